@@ -1,0 +1,415 @@
+"""Benchmark: W4A16 MoE layer tok/s and % HBM roofline over the decode sweep
+(E=256, H=2048, I=512, top-8, sigmoid-gated shared expert,
+GPTQ int4 g128, M in {1,2,4,...,256}) on synthetic seeded weights and inputs.
+
+One step = one layer forward at every M of the sweep, each through L layers of
+distinct weights in sequence (a CUDA graph per M). Every layer call has fresh
+router logits, and the L layers (L x 418 MB) and the sweep's traffic exceed the
+126 MB L2, so weights come from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0). Multi-GPU: one process per GPU (torchrun),
+independent replicas (the decode layer does not shard), weak scaling, time =
+max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SWEEP = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+METRIC = "W4A16 MoE layer tok/s and % HBM roofline, M=1-256; prefetch hit rate"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# CPU reference path (the reference's torch form; the oracle port)
+# ---------------------------------------------------------------------------
+class CpuReference:
+    """The reference CPU path: per-token routed SiLU-MLP + sigmoid-gated shared
+    expert with weights dequantised once to bf16 (the reference's
+    load_topk_expert_mlp + moe_tokens form), torch on all host threads."""
+
+    def __init__(self, tokens=(1, 4, 16)):
+        import torch
+
+        from mtp_b200.synthetic import CONFIG1, make_inputs, make_layer
+        from oracle import layer as olayer
+        from oracle import router as orouter
+
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        experts, shared = make_layer(CONFIG1, seed=0)
+        self.o = olayer.MoeLayerOracle(experts, shared, dtype=torch.bfloat16)
+        self.tokens = tokens
+        self.batches = []
+        t0 = time.perf_counter()
+        for m in tokens:
+            x, logits = make_inputs(CONFIG1, m, seed=100 + m)
+            w, ids, _ = orouter.topk_softmax(logits.numpy(), CONFIG1.top_k, True)
+            self.o.prepare(ids)
+            self.batches.append((m, x, torch.from_numpy(ids), torch.from_numpy(w)))
+        self.dequant_s = time.perf_counter() - t0
+
+    def run(self, seconds: float):
+        tok, el, calls = 0, 0.0, 0
+        deadline = time.perf_counter() + seconds
+        while time.perf_counter() < deadline or calls == 0:
+            for m, x, ids, w in self.batches:
+                t0 = time.perf_counter()
+                self.o.moe_tokens(x, ids, w)
+                el += time.perf_counter() - t0
+                tok += m
+                calls += 1
+        return {
+            "value": tok / el, "unit": UNIT, "cores": self.threads, "kind": "port",
+            "sample": (f"config-1 layer, M in {list(self.tokens)}, {calls} layer calls, {el:.1f} s; bf16 weights "
+                       f"dequantised once ({self.dequant_s:.1f} s, excluded); CPU {cpu_model()}"),
+        }
+
+
+def cpu_reference(seconds: float = 12.0):
+    return CpuReference().run(seconds)
+
+
+# ---------------------------------------------------------------------------
+# GPU path
+# ---------------------------------------------------------------------------
+def algorithmic_bytes(num_unique: int, m: int, cfg, expert_bytes: int) -> int:
+    weights = (num_unique + (1 if cfg.shared else 0)) * expert_bytes
+    acts = m * cfg.hidden * 2 + m * cfg.num_experts * 4 + m * cfg.hidden * 2
+    return weights + acts
+
+
+def run_gpu(args, rank: int, world: int):
+    import numpy as np
+    import torch
+
+    import mtp_b200
+    from mtp_b200.ops import SharedExpert, W4A16Experts, layer_workspace
+    from mtp_b200.synthetic import CONFIG1, make_inputs, make_layer
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = CONFIG1
+    keys = ("w13_qweight", "w13_qzeros", "w13_scales", "w2_qweight", "w2_qzeros", "w2_scales")
+    layers = []
+    for l in range(args.layers):
+        ex, sh = make_layer(cfg, seed=1000 * rank + l, device=dev)
+        w = W4A16Experts.from_gptq(*(ex[k] for k in keys), group_size=cfg.group_size)
+        s = SharedExpert.from_gptq(*(sh[k] for k in keys), sh["gate_weight"], group_size=cfg.group_size)
+        del ex, sh
+        layers.append((w, s))
+    torch.cuda.synchronize()
+    expert_bytes = layers[0][0].expert_bytes
+
+    sweep = [int(v) for v in args.sweep.split(",")]
+    # per-M inputs for every layer; routing differs per layer and per M
+    state = {}
+    for m in sweep:
+        xs, lgs, outs, wss, ids = [], [], [], [], []
+        for l in range(args.layers):
+            x, lg = make_inputs(cfg, m, seed=10_000 * rank + 100 * l + m, device=dev)
+            xs.append(x)
+            lgs.append(lg)
+            outs.append(torch.empty((m, cfg.hidden), dtype=torch.bfloat16, device=dev))
+            wss.append(layer_workspace(m, layers[l][0], cfg.top_k, dev))
+            ids.append(torch.empty((m, cfg.top_k), dtype=torch.int32, device=dev))
+        state[m] = dict(x=xs, logits=lgs, out=outs, ws=wss, ids=ids,
+                        tw=[torch.empty((m, cfg.top_k), device=dev) for _ in range(args.layers)])
+
+    def run_m(m):
+        st = state[m]
+        for l in range(args.layers):
+            w, s = layers[l]
+            mtp_b200.moe_layer_w4a16(st["x"][l], st["logits"][l], w, cfg.top_k, shared=s, out=st["out"][l],
+                                     workspace=st["ws"][l], topk_out=(st["tw"][l], st["ids"][l]))
+
+    # eager warm-up, then one CUDA graph per M (the L layers in sequence)
+    for m in sweep:
+        run_m(m)
+    torch.cuda.synchronize()
+    graphs = {}
+    cap_stream = torch.cuda.Stream(dev)
+    for m in sweep:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap_stream):
+            run_m(m)
+        graphs[m] = g
+    torch.cuda.synchronize()
+
+    # unique experts per (M, layer) for the algorithmic bytes
+    uniq = {m: [int(torch.unique(state[m]["ids"][l]).numel()) for l in range(args.layers)] for m in sweep}
+    bytes_per_m = {m: sum(algorithmic_bytes(u, m, cfg, expert_bytes) for u in uniq[m]) for m in sweep}
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        for m in sweep:
+            graphs[m].replay()
+    torch.cuda.synchronize()
+
+    ev = {m: [] for m in sweep}
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for _ in range(args.steps):
+            for m in sweep:
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                graphs[m].replay()
+                b.record(stream)
+                ev[m].append((a, b))
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    per_m_ms = {m: sum(a.elapsed_time(b) for a, b in ev[m]) / args.steps for m in sweep}
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    hbm_gbs, peak_kind = peaks()
+    tokens_per_step = sum(m * args.layers for m in sweep)
+    value = tokens_per_step * args.steps * world / (elapsed_ms / 1e3)
+    rows = []
+    for m in sweep:
+        us_layer = per_m_ms[m] * 1e3 / args.layers
+        gbs = bytes_per_m[m] / (per_m_ms[m] / 1e3) / 1e9
+        rows.append({"M": m, "us_per_layer": round(us_layer, 3), "tok_s": round(m / (us_layer / 1e6), 1),
+                     "unique_experts": round(sum(uniq[m]) / args.layers, 2),
+                     "bytes_per_layer": bytes_per_m[m] // args.layers, "hbm_gbs": round(gbs, 1),
+                     "hbm_frac": round(gbs / hbm_gbs, 4)})
+    total_bytes = sum(bytes_per_m.values())
+    total_ms = sum(per_m_ms.values())
+    achieved = total_bytes / (total_ms / 1e3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("layer_step_bytes")
+
+    # end to end through the public API with host buffers (pinned), copies timed
+    e2e = run_e2e(args, layers, cfg, sweep, dev, state) if not args.no_e2e else None
+
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1 decode sweep: W4A16 MoE layer E=256 H=2048 I=512 top-8 + shared expert, "
+                               "GPTQ int4 g128 (raw zeros read)",
+                   "tokens": sweep, "layers_per_graph": args.layers, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: L distinct layers (L x 418 MB) and fresh routing per call"},
+        "sweep": rows,
+        "roofline": {"bound": "hbm", "kernel": "w4a16_moe_layer (router+align+W1+W2+combine), all sweep M",
+                     "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
+                     "frac": round(achieved / hbm_gbs, 4), "peak_source": peak_kind,
+                     "traffic": traffic},
+        "gpu_launches": args.steps * len(sweep) * args.layers * 5,
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        result["e2e"] = e2e
+    return result
+
+
+def run_e2e(args, layers, cfg, sweep, dev, state):
+    """Same metric through the public call with pinned host inputs: per layer
+    call H2D of hidden states + router logits, the layer, D2H of the output."""
+    import torch
+
+    import mtp_b200
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    host = {}
+    for m in sweep:
+        hx = [t.cpu().pin_memory() for t in state[m]["x"]]
+        hl = [t.cpu().pin_memory() for t in state[m]["logits"]]
+        ho = [torch.empty((m, cfg.hidden), dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+        dx = [torch.empty_like(t, device=dev) for t in hx]
+        dl = [torch.empty_like(t, device=dev) for t in hl]
+        host[m] = (hx, hl, ho, dx, dl)
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step():
+        for m in sweep:
+            hx, hl, ho, dx, dl = host[m]
+            for l in range(args.layers):
+                dx[l].copy_(hx[l], non_blocking=True)
+                dl[l].copy_(hl[l], non_blocking=True)
+                w, s = layers[l]
+                out = mtp_b200.moe_layer_w4a16(dx[l], dl[l], w, cfg.top_k, shared=s, out=state[m]["out"][l],
+                                               workspace=state[m]["ws"][l])
+                ho[l].copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        one_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    tok = sum(m * args.layers for m in sweep) * steps
+    h2d = sum(m * cfg.hidden * 2 + m * cfg.num_experts * 4 for m in sweep) * args.layers
+    d2h = sum(m * cfg.hidden * 2 for m in sweep) * args.layers
+    return {"value": round(tok / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps,
+            "path": "mtp_b200.moe_layer_w4a16 per layer call (ctypes C-ABI), pinned host in/out, eager launches"}
+
+
+def run_reference(args, rank: int):
+    """``--impl reference``: the reference CPU path alone, rank 0 only."""
+    if rank != 0:
+        return None
+    ref = CpuReference()
+    per_step = min(8.0, max(0.2, 90.0 / max(1, args.steps + args.warmup)))
+    vals, res = [], None
+    for i in range(args.warmup + args.steps):
+        res = ref.run(per_step)
+        if i >= args.warmup:
+            vals.append(res["value"])
+    value = statistics.median(vals)
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config1 decode layer (reference CPU torch path, bounded sample per step)",
+                   "tokens": list(ref.tokens)},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": res["cores"], "kind": res["kind"],
+                         "sample": res["sample"]},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mtp_b200", choices=["mtp_b200", "reference"])
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--sweep", default=",".join(str(m) for m in SWEEP))
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    res = run_gpu(args, rank, world)
+    if rank == 0 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_reference(seconds=args.cpu_seconds)
+    if world > 1:
+        import torch
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

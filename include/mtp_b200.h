@@ -1,0 +1,185 @@
+/*
+ * mtp_b200 - B200 (sm_100a) W4A16 mixture-of-experts layer and expert-prefetch
+ * path: the C ABI.
+ *
+ * Every entry point takes plain pointers and sizes, returns an int status
+ * (0 = MTP_OK, a distinct non-zero code per failure class, never an exception)
+ * and, where it launches GPU work, runs asynchronously on the caller's stream
+ * (`stream` is a cudaStream_t passed as void*; NULL = the legacy default
+ * stream). The caller allocates every output and workspace; the prefetch
+ * session alone owns device state and a side stream.
+ *
+ * Reference interfaces replaced (paths relative to the reference project,
+ * HUSRCF/MTP "mtp-expert-prefetch"; vLLM 0.22.0 paths relative to the package):
+ *   mtp_router_topk            <- vLLM torch.ops._moe_C.topk_softmax, restated by
+ *                                 the reference at tracing/vllm_router_trace.py:4201-4227
+ *   mtp_moe_align              <- vLLM fused_moe/moe_align_block_size.py
+ *                                 moe_align_block_size(), called at
+ *                                 vllm_router_trace.py:19648-19659 (replaced there
+ *                                 through _prepare_expert_assignment, :20083)
+ *   mtp_gptq_dequant           <- repack/gptq_unpack.py:88-131
+ *                                 dequantize_gptq_projection()
+ *   mtp_w4a16_repack_gptq      <- vLLM moe_wna16.py GPTQ weight conversion
+ *                                 (qweight.T -> [E, N, K/2] uint8) consumed by
+ *                                 tracing/vllm_wna16_group_plan.py:242-486
+ *   mtp_w4a16_moe_layer        <- vLLM fused_experts_impl as restated at
+ *                                 vllm_router_trace.py:19330-19840 (W1 at 19674,
+ *                                 activation 19714, W2 at 19761, moe_sum 19801),
+ *                                 the shared-expert gate at 3994-4031 / 4140-4152,
+ *                                 and the CPU forms TopKExpertMlp.forward
+ *                                 (repack/gptq_unpack.py:293-327) and
+ *                                 MtpExtraRunner.moe_tokens (mtp/extra_tensors.py:544-598);
+ *                                 the expert->slot indirection follows the
+ *                                 expert_map reads at vllm_wna16_group_plan.py:87-95,
+ *                                 1555-1567 and the premap slot plan at
+ *                                 runtime/premap.py:223-294
+ *   mtp_predictor_topk         <- training/hidden_residual.py:44-134 forward +
+ *                                 topk as in training/predictor.py:105
+ *   mtp_prefetch_session_*     <- the native producer session C ABI at
+ *                                 microbench/premap_kernel_consumer/
+ *                                 premap_payload_cache_inprocess_native_producer_stub.hip:505-960
+ *                                 (create / destroy / update with int codes and an
+ *                                 opaque u64 handle) and the counter semantics of
+ *                                 runtime/cache_manager.py:193-578
+ */
+#ifndef MTP_B200_H_
+#define MTP_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MTP_API __attribute__((visibility("default")))
+#else
+#define MTP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+enum MtpStatus {
+  MTP_OK = 0,
+  MTP_ERR_NULL = 1,       /* a required pointer is NULL                       */
+  MTP_ERR_SHAPE = 2,      /* a size is out of range or not supported         */
+  MTP_ERR_ALIGN = 3,      /* a pointer is not aligned as the kernel requires  */
+  MTP_ERR_WORKSPACE = 4,  /* workspace smaller than the size query returned   */
+  MTP_ERR_LAUNCH = 5,     /* a kernel launch failed                           */
+  MTP_ERR_CUDA = 6,       /* another CUDA runtime call failed                 */
+  MTP_ERR_HANDLE = 7,     /* bad or destroyed session handle                  */
+  MTP_ERR_CAPACITY = 8,   /* no free slot / ring full                         */
+  MTP_ERR_ARG = 9         /* an enum or flag argument has an unknown value    */
+};
+
+MTP_API const char* mtp_status_string(int status);
+MTP_API int mtp_abi_version(void);
+
+/* ---- router (softmax -> top-k -> renormalise) ----------------------------- */
+/* logits [M, E] fp32 -> topk_weights [M, k] fp32, topk_ids [M, k] int32
+ * (descending; exact ties -> lower expert id), token_expert_indices [M, k]
+ * (= j, as the reference fallback writes; may be NULL). renormalize: w/sum(w)
+ * with the sum clamped to 1e-20. 1 <= k <= 32, 1 <= E <= 1024.               */
+MTP_API int mtp_router_topk(const float* logits, int32_t M, int32_t E, int32_t k,
+                    int32_t renormalize, float* topk_weights, int32_t* topk_ids,
+                    int32_t* token_expert_indices, void* stream);
+
+/* ---- moe_align_block_size (canonical order) ------------------------------- */
+/* Buffer sizes exactly as vLLM's wrapper computes them.                      */
+MTP_API int mtp_moe_align_sizes(int32_t numel, int32_t num_experts, int32_t block_size,
+                        int32_t pad_sorted_ids, int32_t* sorted_capacity,
+                        int32_t* max_blocks, int32_t* max_segments);
+/* topk_ids [numel] int32 -> sorted_token_ids [sorted_capacity] (sentinel numel),
+ * expert_ids [max_blocks] (-1 past the last used block), num_tokens_post_padded
+ * [1]; within an expert the flat pair index ascends. expert_map [E] may be
+ * NULL. segments (may be NULL) receives [max_segments][3] rows
+ * (expert, first_block, block_count) and num_segments [1] their count.       */
+MTP_API int mtp_moe_align(const int32_t* topk_ids, int32_t numel, int32_t num_experts,
+                  int32_t block_size, const int32_t* expert_map,
+                  int32_t ignore_invalid_experts, int32_t pad_sorted_ids,
+                  int32_t* sorted_token_ids, int32_t* expert_ids,
+                  int32_t* num_tokens_post_padded, int32_t* segments,
+                  int32_t* num_segments, void* stream);
+
+/* ---- GPTQ int4 weights ----------------------------------------------------- */
+enum MtpZeroMode {
+  MTP_ZERO_RAW = 0,   /* (q - stored zero) * scale: the reference torch oracle */
+  MTP_ZERO_SYM8 = 1   /* (q - 8) * scale, stored zeros ignored: vLLM sym GPTQ */
+};
+
+/* fp32 dequantisation of one projection, GPTQ checkpoint form:
+ * qweight [K/8, N] int32, qzeros [K/G, N/8] int32, scales [K/G, N] fp16 (bits),
+ * g_idx [K] int32 or NULL (= k / G). out [N, K] fp32 (Linear orientation).   */
+MTP_API int mtp_gptq_dequant(const int32_t* qweight, const int32_t* qzeros,
+                     const uint16_t* scales, const int32_t* g_idx, int32_t K,
+                     int32_t N, int32_t group_size, int32_t zero_mode,
+                     float* out, void* stream);
+
+/* Byte offsets of the sections of one expert blob in the kernel layout:
+ * [w13 weights | w13 scales | w13 zeros | w2 weights | w2 scales | w2 zeros],
+ * w13 = gate rows then up rows, [2I, H]; w2 = [H, I]. Every section starts on
+ * a 256-byte boundary; `bytes` is the blob stride.                            */
+typedef struct MtpExpertLayout {
+  int64_t w13_qweight, w13_scales, w13_zeros;
+  int64_t w2_qweight, w2_scales, w2_zeros;
+  int64_t bytes;
+} MtpExpertLayout;
+MTP_API int mtp_w4a16_expert_layout(int32_t hidden, int32_t inter, int32_t group_size,
+                            MtpExpertLayout* out);
+
+/* Repack E experts from the GPTQ checkpoint form (stacked on a leading E axis:
+ * w13 qweight [E, H/8, 2I], qzeros [E, H/G, 2I/8], scales [E, H/G, 2I];
+ * w2 qweight [E, I/8, H], qzeros [E, I/G, H/8], scales [E, I/G, H]) into
+ * out_blobs [E, layout.bytes].                                              */
+MTP_API int mtp_w4a16_repack_gptq(const int32_t* w13_qweight, const int32_t* w13_qzeros,
+                          const uint16_t* w13_scales, const int32_t* w2_qweight,
+                          const int32_t* w2_qzeros, const uint16_t* w2_scales,
+                          int32_t num_experts, int32_t hidden, int32_t inter,
+                          int32_t group_size, uint8_t* out_blobs, void* stream);
+
+/* ---- the MoE layer forward ------------------------------------------------- */
+typedef struct MtpMoeLayerArgs {
+  int32_t num_tokens;        /* M >= 1                                        */
+  int32_t hidden;            /* H: multiple of 256, <= 8192                   */
+  int32_t inter;             /* I: multiple of 64                             */
+  int32_t num_experts;       /* E: 1..1024 (global expert count)              */
+  int32_t top_k;             /* 1..32                                         */
+  int32_t group_size;        /* 64 or 128                                     */
+  int32_t renormalize;       /* router: renormalise the top-k weights         */
+  int32_t zero_mode;         /* MtpZeroMode                                   */
+  const uint16_t* hidden_states;   /* [M, H] bf16                             */
+  const float* router_logits;      /* [M, E] fp32; NULL -> use topk_* below   */
+  const float* topk_weights;       /* [M, k] fp32 (when router_logits NULL)   */
+  const int32_t* topk_ids;         /* [M, k] int32 (when router_logits NULL)  */
+  const uint8_t* expert_blobs;     /* resident experts: slot s at
+                                      expert_blobs + s * expert_bytes         */
+  int64_t expert_bytes;            /* mtp_w4a16_expert_layout().bytes         */
+  const int32_t* slot_table;       /* [E] expert -> slot, -1 = not resident;
+                                      NULL -> slot = expert                   */
+  const uint8_t* host_blobs;       /* device-visible pinned host store, expert
+                                      e at host_blobs + e * expert_bytes, read
+                                      for slot -1 (demand fetch); may be NULL */
+  const uint8_t* shared_blob;      /* shared expert blob or NULL              */
+  const uint16_t* shared_gate_weight; /* [H] bf16, required with shared_blob  */
+  uint16_t* out;                   /* [M, H] bf16                             */
+  float* out_f32;                  /* optional [M, H] fp32 copy (may be NULL) */
+  float* topk_weights_out;         /* optional [M, k] router weights          */
+  int32_t* topk_ids_out;           /* optional [M, k] router ids              */
+  int32_t* demand_log;             /* optional [1 + min(E, M*k)]: count, then
+                                      the distinct experts demanded, ascending */
+  int32_t* status;                 /* optional [4]: [0] slot misses served from
+                                      host_blobs, [1] misses with no host store
+                                      (expert output zeroed), [2],[3] reserved;
+                                      accumulated, the caller zeroes it        */
+  void* workspace;
+  int64_t workspace_bytes;
+} MtpMoeLayerArgs;
+
+MTP_API int mtp_w4a16_moe_layer_workspace_size(int32_t num_tokens, int32_t num_experts,
+                                       int32_t top_k, int32_t hidden,
+                                       int32_t inter, int64_t* bytes);
+MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MTP_B200_H_ */

@@ -1,0 +1,120 @@
+"""ctypes binding of libmtp_b200.so (the C ABI declared in include/mtp_b200.h).
+
+The library is loaded from the package's ``lib/`` directory, where
+``python -m mtp_b200.build`` (or ``__graft_entry__.build()``) puts it. There is
+no fallback: if the library is missing or does not load, every operation
+raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmtp_b200.so"
+
+# Every symbol include/mtp_b200.h declares (checked by the tests).
+EXPORTS = (
+    "mtp_status_string",
+    "mtp_abi_version",
+    "mtp_router_topk",
+    "mtp_moe_align_sizes",
+    "mtp_moe_align",
+    "mtp_gptq_dequant",
+    "mtp_w4a16_expert_layout",
+    "mtp_w4a16_repack_gptq",
+    "mtp_w4a16_moe_layer_workspace_size",
+    "mtp_w4a16_moe_layer",
+)
+
+MTP_ZERO_RAW = 0
+MTP_ZERO_SYM8 = 1
+
+vp = C.c_void_p
+i32 = C.c_int32
+i64 = C.c_int64
+
+
+class MtpExpertLayout(C.Structure):
+    _fields_ = [("w13_qweight", i64), ("w13_scales", i64), ("w13_zeros", i64),
+                ("w2_qweight", i64), ("w2_scales", i64), ("w2_zeros", i64), ("bytes", i64)]
+
+
+class MtpMoeLayerArgs(C.Structure):
+    _fields_ = [
+        ("num_tokens", i32), ("hidden", i32), ("inter", i32), ("num_experts", i32),
+        ("top_k", i32), ("group_size", i32), ("renormalize", i32), ("zero_mode", i32),
+        ("hidden_states", vp), ("router_logits", vp), ("topk_weights", vp), ("topk_ids", vp),
+        ("expert_blobs", vp), ("expert_bytes", i64), ("slot_table", vp), ("host_blobs", vp),
+        ("shared_blob", vp), ("shared_gate_weight", vp), ("out", vp), ("out_f32", vp),
+        ("topk_weights_out", vp), ("topk_ids_out", vp), ("demand_log", vp), ("status", vp),
+        ("workspace", vp), ("workspace_bytes", i64),
+    ]
+
+
+_SIGS = {
+    "mtp_status_string": (C.c_char_p, [C.c_int]),
+    "mtp_abi_version": (C.c_int, []),
+    "mtp_router_topk": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, vp, vp]),
+    "mtp_moe_align_sizes": (C.c_int, [i32, i32, i32, i32, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
+    "mtp_moe_align": (C.c_int, [vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp, vp, vp]),
+    "mtp_gptq_dequant": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp]),
+    "mtp_w4a16_expert_layout": (C.c_int, [i32, i32, i32, C.POINTER(MtpExpertLayout)]),
+    "mtp_w4a16_repack_gptq": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp]),
+    "mtp_w4a16_moe_layer_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
+    "mtp_w4a16_moe_layer": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class MtpError(RuntimeError):
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} failed with status {status}: {message}")
+        self.status = status
+
+
+def load() -> C.CDLL:
+    """Load (once) and return the library; raises if it is absent."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise ImportError(
+                    f"{LIB_PATH} is missing: build it with `python -m mtp_b200.build` "
+                    "(there is no CPU fallback for mtp_b200 operations)")
+            lib = C.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        msg = lib.mtp_status_string(status).decode()
+        raise MtpError(name, status, msg)
+
+
+def expert_layout(hidden: int, inter: int, group_size: int) -> MtpExpertLayout:
+    out = MtpExpertLayout()
+    call("mtp_w4a16_expert_layout", hidden, inter, group_size, C.byref(out))
+    return out
+
+
+def align_sizes(numel: int, num_experts: int, block_size: int, pad_sorted_ids: bool = False):
+    cap, blocks, segs = i32(), i32(), i32()
+    call("mtp_moe_align_sizes", numel, num_experts, block_size, int(pad_sorted_ids),
+         C.byref(cap), C.byref(blocks), C.byref(segs))
+    return cap.value, blocks.value, segs.value
+
+
+def layer_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> int:
+    out = i64()
+    call("mtp_w4a16_moe_layer_workspace_size", m, e, k, hidden, inter, C.byref(out))
+    return out.value

@@ -1,0 +1,226 @@
+// extern "C" entry points of libmtp_b200: argument checks, workspace carving,
+// launch order. Every function returns an MtpStatus; nothing throws.
+#include "internal.cuh"
+
+#include <algorithm>
+
+namespace mtp {
+
+constexpr int kLayerBM = 8;
+
+struct AlignSizes {
+  int cap, max_blocks, max_seg;
+};
+
+static AlignSizes align_sizes(int numel, int E, int BM, int pad) {
+  int64_t cap = static_cast<int64_t>(numel) + static_cast<int64_t>(E) * (BM - 1);
+  if (pad) cap = round_up(cap, BM);
+  if (numel < E) cap = std::min<int64_t>(static_cast<int64_t>(numel) * BM, cap);
+  AlignSizes s;
+  s.cap = static_cast<int>(cap);
+  s.max_blocks = static_cast<int>((cap + BM - 1) / BM);
+  s.max_seg = std::min(numel, E);
+  return s;
+}
+
+// Workspace of the layer call, each region 256-byte aligned.
+struct LayerWs {
+  int64_t tw, tid, sorted, eids, ntpp, segs, nseg, hbuf, ybuf, total;
+};
+
+static LayerWs layer_ws(int M, int E, int k, int H, int I) {
+  const int numel = M * k;
+  const AlignSizes s = align_sizes(numel, E, kLayerBM, 0);
+  LayerWs w;
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t at = o;
+    o = round_up(o + bytes, 256);
+    return at;
+  };
+  w.tw = take(4LL * numel);
+  w.tid = take(4LL * numel);
+  w.sorted = take(4LL * s.cap);
+  w.eids = take(4LL * s.max_blocks);
+  w.ntpp = take(4);
+  w.segs = take(12LL * s.max_seg);
+  w.nseg = take(4);
+  w.hbuf = take(2LL * (numel + M) * I);
+  w.ybuf = take(4LL * (numel + M) * H);
+  w.total = o;
+  return w;
+}
+
+}  // namespace mtp
+
+using namespace mtp;
+
+extern "C" {
+
+const char* mtp_status_string(int status) {
+  switch (status) {
+    case MTP_OK: return "ok";
+    case MTP_ERR_NULL: return "required pointer is NULL";
+    case MTP_ERR_SHAPE: return "size out of range or unsupported";
+    case MTP_ERR_ALIGN: return "pointer misaligned";
+    case MTP_ERR_WORKSPACE: return "workspace too small";
+    case MTP_ERR_LAUNCH: return "kernel launch failed";
+    case MTP_ERR_CUDA: return "CUDA runtime call failed";
+    case MTP_ERR_HANDLE: return "bad session handle";
+    case MTP_ERR_CAPACITY: return "capacity exhausted";
+    case MTP_ERR_ARG: return "unknown enum/flag value";
+    default: return "unknown status";
+  }
+}
+
+int mtp_abi_version(void) { return 1; }
+
+int mtp_router_topk(const float* logits, int32_t M, int32_t E, int32_t k, int32_t renormalize,
+                    float* topk_weights, int32_t* topk_ids, int32_t* token_expert_indices,
+                    void* stream) {
+  if (!logits || !topk_weights || !topk_ids) return MTP_ERR_NULL;
+  if (M < 0 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return MTP_ERR_SHAPE;
+  if (M == 0) return MTP_OK;
+  return launch_router_topk(logits, M, E, k, renormalize ? 1 : 0, topk_weights, topk_ids,
+                            token_expert_indices, static_cast<cudaStream_t>(stream));
+}
+
+int mtp_moe_align_sizes(int32_t numel, int32_t num_experts, int32_t block_size,
+                        int32_t pad_sorted_ids, int32_t* sorted_capacity, int32_t* max_blocks,
+                        int32_t* max_segments) {
+  if (!sorted_capacity || !max_blocks) return MTP_ERR_NULL;
+  if (numel < 0 || num_experts < 1 || block_size < 1) return MTP_ERR_SHAPE;
+  const AlignSizes s = align_sizes(numel, num_experts, block_size, pad_sorted_ids);
+  *sorted_capacity = s.cap;
+  *max_blocks = s.max_blocks;
+  if (max_segments) *max_segments = s.max_seg;
+  return MTP_OK;
+}
+
+int mtp_moe_align(const int32_t* topk_ids, int32_t numel, int32_t num_experts, int32_t block_size,
+                  const int32_t* expert_map, int32_t ignore_invalid_experts, int32_t pad_sorted_ids,
+                  int32_t* sorted_token_ids, int32_t* expert_ids, int32_t* num_tokens_post_padded,
+                  int32_t* segments, int32_t* num_segments, void* stream) {
+  if (!sorted_token_ids || !expert_ids || !num_tokens_post_padded) return MTP_ERR_NULL;
+  if (numel > 0 && !topk_ids) return MTP_ERR_NULL;
+  if ((segments == nullptr) != (num_segments == nullptr)) return MTP_ERR_NULL;
+  if (numel < 0 || num_experts < 1 || num_experts > 1024 || block_size < 1 || block_size > 1024)
+    return MTP_ERR_SHAPE;
+  const AlignSizes s = align_sizes(numel, num_experts, block_size, pad_sorted_ids);
+  return launch_moe_align(topk_ids, numel, num_experts, block_size, expert_map,
+                          ignore_invalid_experts ? 1 : 0, s.cap, s.max_blocks, s.max_seg,
+                          sorted_token_ids, expert_ids, num_tokens_post_padded, segments,
+                          num_segments, static_cast<cudaStream_t>(stream));
+}
+
+int mtp_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                     const int32_t* g_idx, int32_t K, int32_t N, int32_t group_size,
+                     int32_t zero_mode, float* out, void* stream) {
+  if (!qweight || !scales || !out) return MTP_ERR_NULL;
+  if (zero_mode != MTP_ZERO_RAW && zero_mode != MTP_ZERO_SYM8) return MTP_ERR_ARG;
+  if (zero_mode == MTP_ZERO_RAW && !qzeros) return MTP_ERR_NULL;
+  if (K <= 0 || N <= 0 || K % 8 || N % 8 || group_size <= 0 || K % group_size) return MTP_ERR_SHAPE;
+  return gptq_dequant(qweight, qzeros, scales, g_idx, K, N, group_size, zero_mode, out,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int mtp_w4a16_expert_layout(int32_t hidden, int32_t inter, int32_t group_size, MtpExpertLayout* out) {
+  if (!out) return MTP_ERR_NULL;
+  if (hidden <= 0 || inter <= 0 || hidden % 64 || inter % 64 || group_size % 64 ||
+      hidden % group_size || inter % group_size)
+    return MTP_ERR_SHAPE;
+  return expert_layout(hidden, inter, group_size, out);
+}
+
+int mtp_w4a16_repack_gptq(const int32_t* w13_qweight, const int32_t* w13_qzeros,
+                          const uint16_t* w13_scales, const int32_t* w2_qweight,
+                          const int32_t* w2_qzeros, const uint16_t* w2_scales, int32_t num_experts,
+                          int32_t hidden, int32_t inter, int32_t group_size, uint8_t* out_blobs,
+                          void* stream) {
+  if (!w13_qweight || !w13_qzeros || !w13_scales || !w2_qweight || !w2_qzeros || !w2_scales ||
+      !out_blobs)
+    return MTP_ERR_NULL;
+  MtpExpertLayout L;
+  const int r = mtp_w4a16_expert_layout(hidden, inter, group_size, &L);
+  if (r != MTP_OK) return r;
+  if (num_experts <= 0) return MTP_ERR_SHAPE;
+  if (!aligned(out_blobs, 256)) return MTP_ERR_ALIGN;
+  return repack_gptq(w13_qweight, w13_qzeros, w13_scales, w2_qweight, w2_qzeros, w2_scales,
+                     num_experts, hidden, inter, group_size, out_blobs,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int mtp_w4a16_moe_layer_workspace_size(int32_t num_tokens, int32_t num_experts, int32_t top_k,
+                                       int32_t hidden, int32_t inter, int64_t* bytes) {
+  if (!bytes) return MTP_ERR_NULL;
+  if (num_tokens < 1 || num_experts < 1 || top_k < 1 || hidden < 1 || inter < 1) return MTP_ERR_SHAPE;
+  *bytes = layer_ws(num_tokens, num_experts, top_k, hidden, inter).total;
+  return MTP_OK;
+}
+
+int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
+  if (!p) return MTP_ERR_NULL;
+  const MtpMoeLayerArgs& a = *p;
+  const int M = a.num_tokens, H = a.hidden, I = a.inter, E = a.num_experts, k = a.top_k;
+  const int G = a.group_size;
+  if (M < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return MTP_ERR_SHAPE;
+  if (H < 256 || H > 2048 || H % 256) return MTP_ERR_SHAPE;
+  if (I < 64 || I > 1024 || I % 64) return MTP_ERR_SHAPE;
+  if (G != 64 && G != 128) return MTP_ERR_SHAPE;
+  if (I % G || H % G) return MTP_ERR_SHAPE;
+  if (a.zero_mode != MTP_ZERO_RAW && a.zero_mode != MTP_ZERO_SYM8) return MTP_ERR_ARG;
+  if (!a.hidden_states || !a.out || !a.workspace) return MTP_ERR_NULL;
+  if (!a.expert_blobs && !(a.slot_table && a.host_blobs)) return MTP_ERR_NULL;
+  if (!a.router_logits && (!a.topk_weights || !a.topk_ids)) return MTP_ERR_NULL;
+  if (a.shared_blob && !a.shared_gate_weight) return MTP_ERR_NULL;
+  MtpExpertLayout L;
+  if (expert_layout(H, I, G, &L) != MTP_OK) return MTP_ERR_SHAPE;
+  if (a.expert_bytes < L.bytes) return MTP_ERR_SHAPE;
+  if (!aligned(a.hidden_states, 16) || !aligned(a.out, 8) || !aligned(a.workspace, 256) ||
+      (a.expert_blobs && !aligned(a.expert_blobs, 256)) || (a.expert_bytes % 256) ||
+      (a.host_blobs && !aligned(a.host_blobs, 256)) ||
+      (a.shared_blob && !aligned(a.shared_blob, 256)) || (a.out_f32 && !aligned(a.out_f32, 16)))
+    return MTP_ERR_ALIGN;
+  const LayerWs w = layer_ws(M, E, k, H, I);
+  if (a.workspace_bytes < w.total) return MTP_ERR_WORKSPACE;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned char* ws = static_cast<unsigned char*>(a.workspace);
+  const int numel = M * k;
+  const AlignSizes s = align_sizes(numel, E, kLayerBM, 0);
+
+  const float* tw = a.topk_weights;
+  const int32_t* tid = a.topk_ids;
+  if (a.router_logits) {
+    float* w_out = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
+    int32_t* i_out = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
+    int r = launch_router_topk(a.router_logits, M, E, k, a.renormalize ? 1 : 0, w_out, i_out,
+                               nullptr, st);
+    if (r != MTP_OK) return r;
+    tw = w_out;
+    tid = i_out;
+  }
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
+  int32_t* eids = reinterpret_cast<int32_t*>(ws + w.eids);
+  int32_t* ntpp = reinterpret_cast<int32_t*>(ws + w.ntpp);
+  int32_t* segs = reinterpret_cast<int32_t*>(ws + w.segs);
+  int32_t* nseg = reinterpret_cast<int32_t*>(ws + w.nseg);
+  int r = launch_moe_align(tid, numel, E, kLayerBM, nullptr, 0, s.cap, s.max_blocks, s.max_seg,
+                           sorted, eids, ntpp, segs, nseg, st);
+  if (r != MTP_OK) return r;
+
+  MoeDevArgs d;
+  d.M = M; d.H = H; d.I = I; d.E = E; d.k = k; d.zero_mode = a.zero_mode;
+  d.numel = numel; d.max_seg = s.max_seg; d.has_shared = a.shared_blob ? 1 : 0;
+  d.x = a.hidden_states; d.topk_w = tw; d.topk_ids = tid;
+  d.sorted = sorted; d.segs = segs; d.nseg = nseg;
+  d.blobs = a.expert_blobs; d.expert_bytes = a.expert_bytes;
+  d.slot_table = a.slot_table; d.host_blobs = a.host_blobs; d.shared_blob = a.shared_blob;
+  d.L = L;
+  d.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
+  d.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
+  d.status = a.status;
+  return launch_moe_decode(d, G, a.shared_gate_weight, a.out, a.out_f32, a.demand_log, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,142 @@
+// Shared device helpers for the sm_100a kernels of mtp_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "mtp_b200.h"
+
+namespace mtp {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Host-side status helpers
+// ---------------------------------------------------------------------------
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTP_OK : MTP_ERR_LAUNCH;
+}
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// ---------------------------------------------------------------------------
+// Memory access
+// ---------------------------------------------------------------------------
+// 16-byte streaming load that bypasses L1 allocation: expert weights are read
+// exactly once per layer call, so they should not evict reused data.
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_u8(const void* p) {
+  uint16_t r;
+  asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core MMA (m16n8k16, bf16 inputs, fp32 accumulate)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------
+// int4 -> bf16 dequantisation by exponent bias
+// ---------------------------------------------------------------------------
+// A bf16 with bit pattern 0x4300 is 128.0 and has 7 mantissa bits, so OR-ing a
+// nibble q (0..15) into its low mantissa bits gives exactly 128 + q. Subtracting
+// the bf16 value 128 + z (same construction) then yields q - z exactly (an
+// integer in [-15, 15] is representable). Two nibbles are handled per 32-bit
+// register: bits [4j, 4j+4) land in the low half, bits [16+4j, 20+4j) in the
+// high half.
+__device__ __forceinline__ uint32_t nib_pair_biased(uint32_t w, int j) {
+  return ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// Bias constant (128 + z) replicated into both bf16 halves.
+__device__ __forceinline__ uint32_t zero_bias_pair(uint32_t z) {
+  return (0x4300u | (z & 0xFu)) * 0x00010001u;
+}
+
+// One packed weight word -> the four A-fragment registers of an m16n8k16 tile.
+// Word layout (see gptq.cu, kernel layout): nibble j and nibble j+4 are the two
+// elements of A register j; registers 0 and 2 are the thread's row g, 1 and 3
+// its row g+8. One volatile block so the extraction is not hoisted across the
+// whole unrolled K loop (which would hold every dequantised fragment live).
+// lop3 immediate 0xEA = (a & b) | c.
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t zb_lo, uint32_t zb_hi,
+                                             uint32_t (&a)[4]) {
+  asm volatile(
+      "{\n"
+      ".reg .b32 t0, t1, t2, t3;\n"
+      "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n"
+      "shr.u32 t1, %4, 4;\n"
+      "lop3.b32 t1, t1, 0x000F000F, 0x43004300, 0xEA;\n"
+      "shr.u32 t2, %4, 8;\n"
+      "lop3.b32 t2, t2, 0x000F000F, 0x43004300, 0xEA;\n"
+      "shr.u32 t3, %4, 12;\n"
+      "lop3.b32 t3, t3, 0x000F000F, 0x43004300, 0xEA;\n"
+      "sub.rn.bf16x2 %0, t0, %5;\n"
+      "sub.rn.bf16x2 %1, t1, %6;\n"
+      "sub.rn.bf16x2 %2, t2, %5;\n"
+      "sub.rn.bf16x2 %3, t3, %6;\n"
+      "}\n"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+      : "r"(w), "r"(zb_lo), "r"(zb_hi));
+}
+
+// B fragment of an m16n8k16 tile from a k-permuted shared-memory row (see
+// stage_rows_permuted): one 8-byte load gives (b0, b1). Volatile so the load
+// stays next to its MMA rather than being hoisted (register pressure).
+__device__ __forceinline__ void lds_bfrag(const uint16_t* p, uint32_t* b0, uint32_t* b1) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(*b0), "=r"(*b1) : "r"(a));
+}
+
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t v) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  return __half22float2(h);
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v) << 16);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// Warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFullMask, v, o));
+  return v;
+}
+
+}  // namespace mtp

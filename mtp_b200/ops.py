@@ -1,0 +1,324 @@
+"""Host API of the W4A16 MoE path: torch tensors in, C-ABI calls out.
+
+Names and argument meanings follow the reference interfaces this path drops
+in for (paths relative to the reference project; vLLM 0.22.0 paths relative to
+the package):
+
+* :func:`topk_softmax`          - vLLM ``topk_softmax`` (restated at
+                                  tracing/vllm_router_trace.py:4201-4227);
+* :func:`moe_align_block_size`  - vLLM ``fused_moe/moe_align_block_size.py``;
+* :func:`dequantize_gptq_projection` - repack/gptq_unpack.py:88-131;
+* :func:`fused_experts`         - vLLM ``fused_experts`` (signature probed by the
+                                  reference, replaced at vllm_router_trace.py:19330-19840);
+* :func:`moe_layer_w4a16`       - router + fused_experts + shared expert, the
+                                  ``FusedMoE.forward_impl`` boundary (17977) and
+                                  ``MtpExtraRunner.moe_tokens`` (mtp/extra_tensors.py:544-598).
+
+Shape and dtype errors raise ``ValueError`` before any launch (as
+gptq_unpack.py:374-417 and the reference invokers do); a non-zero C status
+raises :class:`mtp_b200._lib.MtpError`. Every call is asynchronous on the
+current torch CUDA stream. There is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+ZERO_MODES = {"raw": _lib.MTP_ZERO_RAW, "sym8": _lib.MTP_ZERO_SYM8}
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _check_cuda(name: str, t: torch.Tensor | None, dtype: torch.dtype | None = None, ndim: int | None = None):
+    if t is None:
+        return
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor, got device {t.device}")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if ndim is not None and t.ndim != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# ---------------------------------------------------------------------------
+# router
+# ---------------------------------------------------------------------------
+def topk_softmax(gating_output: torch.Tensor, topk: int, renormalize: bool = True):
+    """softmax -> top-k -> (optional) renormalise. Returns
+    ``(topk_weights fp32 [M,k], topk_ids int32 [M,k], token_expert_indices int32 [M,k])``."""
+    _check_cuda("gating_output", gating_output, torch.float32, 2)
+    m, e = gating_output.shape
+    if not 0 < topk <= min(e, 32):
+        raise ValueError(f"topk must be in [1, {min(e, 32)}], got {topk}")
+    if e > 1024:
+        raise ValueError(f"at most 1024 experts are supported, got {e}")
+    dev = gating_output.device
+    w = torch.empty((m, topk), dtype=torch.float32, device=dev)
+    ids = torch.empty((m, topk), dtype=torch.int32, device=dev)
+    tei = torch.empty((m, topk), dtype=torch.int32, device=dev)
+    if m:
+        _lib.call("mtp_router_topk", _p(gating_output), m, e, topk, int(bool(renormalize)),
+                  _p(w), _p(ids), _p(tei), _stream(gating_output))
+    return w, ids, tei
+
+
+# ---------------------------------------------------------------------------
+# align
+# ---------------------------------------------------------------------------
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
+                         expert_map: torch.Tensor | None = None, pad_sorted_ids: bool = False,
+                         ignore_invalid_experts: bool = False, *, return_segments: bool = False):
+    """Same contract as vLLM's wrapper; the order inside an expert is the
+    ascending flat index ``t*top_k + j`` (deterministic). With
+    ``return_segments`` also returns ``(segments [max_seg, 3], num_segments [1])``."""
+    if topk_ids.dtype != torch.int32:
+        raise ValueError(f"topk_ids must be int32, got {topk_ids.dtype}")
+    _check_cuda("topk_ids", topk_ids)
+    if expert_map is not None:
+        _check_cuda("expert_map", expert_map, torch.int32, 1)
+        if expert_map.numel() != num_experts:
+            raise ValueError("expert_map must have num_experts entries")
+    numel = topk_ids.numel()
+    cap, blocks, max_seg = _lib.align_sizes(numel, num_experts, block_size, pad_sorted_ids)
+    dev = topk_ids.device
+    sorted_ids = torch.empty(cap, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty(blocks, dtype=torch.int32, device=dev)
+    ntpp = torch.empty(1, dtype=torch.int32, device=dev)
+    segs = torch.empty((max(max_seg, 1), 3), dtype=torch.int32, device=dev) if return_segments else None
+    nseg = torch.empty(1, dtype=torch.int32, device=dev) if return_segments else None
+    _lib.call("mtp_moe_align", _p(topk_ids), numel, num_experts, block_size, _p(expert_map),
+              int(bool(ignore_invalid_experts)), int(bool(pad_sorted_ids)), _p(sorted_ids),
+              _p(expert_ids), _p(ntpp), _p(segs), _p(nseg), _stream(topk_ids))
+    if return_segments:
+        return sorted_ids, expert_ids, ntpp, segs[:max_seg], nseg
+    return sorted_ids, expert_ids, ntpp
+
+
+# ---------------------------------------------------------------------------
+# GPTQ weights
+# ---------------------------------------------------------------------------
+def dequantize_gptq_projection(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                               g_idx: torch.Tensor | None = None, *, group_size: int = 128,
+                               zero_mode: str = "raw", dtype: torch.dtype = torch.float32,
+                               linear_weight: bool = True) -> torch.Tensor:
+    """fp32 ``(q - z[g_idx]) * s[g_idx]`` on the GPU; [out, in] when ``linear_weight``."""
+    _check_cuda("qweight", qweight, torch.int32, 2)
+    _check_cuda("qzeros", qzeros, torch.int32, 2)
+    _check_cuda("scales", scales, torch.float16, 2)
+    _check_cuda("g_idx", g_idx, torch.int32, 1)
+    k = qweight.shape[0] * 8
+    n = qweight.shape[1]
+    if scales.shape[1] != n or qzeros.shape[1] * 8 != n or scales.shape != (qzeros.shape[0], n):
+        raise ValueError(f"inconsistent GPTQ shapes: qweight {tuple(qweight.shape)}, "
+                         f"qzeros {tuple(qzeros.shape)}, scales {tuple(scales.shape)}")
+    if g_idx is not None and g_idx.numel() != k:
+        raise ValueError(f"g_idx has {g_idx.numel()} entries, expected {k}")
+    if zero_mode not in ZERO_MODES:
+        raise ValueError(f"zero_mode must be one of {sorted(ZERO_MODES)}")
+    out = torch.empty((n, k), dtype=torch.float32, device=qweight.device)
+    _lib.call("mtp_gptq_dequant", _p(qweight), _p(qzeros), _p(scales.view(torch.int16)), _p(g_idx),
+              k, n, group_size, ZERO_MODES[zero_mode], _p(out), _stream(qweight))
+    if not linear_weight:
+        out = out.t().contiguous()
+    return out.to(dtype)
+
+
+@dataclass
+class W4A16Experts:
+    """E routed experts in the kernel layout: ``blobs`` uint8 [E, layout.bytes]."""
+
+    blobs: torch.Tensor | None
+    num_experts: int
+    hidden: int
+    inter: int
+    group_size: int
+    layout: _lib.MtpExpertLayout
+
+    @property
+    def expert_bytes(self) -> int:
+        return int(self.layout.bytes)
+
+    @classmethod
+    def from_gptq(cls, w13_qweight, w13_qzeros, w13_scales, w2_qweight, w2_qzeros, w2_scales,
+                  *, group_size: int = 128) -> "W4A16Experts":
+        """Repack GPTQ checkpoint tensors (leading E axis) once into the kernel
+        layout. w13 = [gate; up] rows: qweight [E, H/8, 2I]; w2: qweight [E, I/8, H]."""
+        for name, t, dt in (("w13_qweight", w13_qweight, torch.int32), ("w13_qzeros", w13_qzeros, torch.int32),
+                            ("w13_scales", w13_scales, torch.float16), ("w2_qweight", w2_qweight, torch.int32),
+                            ("w2_qzeros", w2_qzeros, torch.int32), ("w2_scales", w2_scales, torch.float16)):
+            _check_cuda(name, t, dt, 3)
+        e, h8, two_i = w13_qweight.shape
+        hidden, inter = h8 * 8, two_i // 2
+        if w2_qweight.shape != (e, inter // 8, hidden):
+            raise ValueError(f"w2_qweight must be {(e, inter // 8, hidden)}, got {tuple(w2_qweight.shape)}")
+        if w13_scales.shape != (e, hidden // group_size, two_i) or w2_scales.shape != (e, inter // group_size, hidden):
+            raise ValueError("scales do not match group_size")
+        if w13_qzeros.shape != (e, hidden // group_size, two_i // 8) or w2_qzeros.shape != (e, inter // group_size, hidden // 8):
+            raise ValueError("qzeros do not match group_size")
+        layout = _lib.expert_layout(hidden, inter, group_size)
+        blobs = torch.empty((e, layout.bytes), dtype=torch.uint8, device=w13_qweight.device)
+        _lib.call("mtp_w4a16_repack_gptq", _p(w13_qweight), _p(w13_qzeros), _p(w13_scales.view(torch.int16)),
+                  _p(w2_qweight), _p(w2_qzeros), _p(w2_scales.view(torch.int16)), e, hidden, inter,
+                  group_size, _p(blobs), _stream(w13_qweight))
+        return cls(blobs, e, hidden, inter, group_size, layout)
+
+
+@dataclass
+class SharedExpert:
+    """The sigmoid-gated shared expert: one blob [layout.bytes] + gate weight [H] bf16."""
+
+    blob: torch.Tensor
+    gate_weight: torch.Tensor
+
+    @classmethod
+    def from_gptq(cls, w13_qweight, w13_qzeros, w13_scales, w2_qweight, w2_qzeros, w2_scales,
+                  gate_weight, *, group_size: int = 128) -> "SharedExpert":
+        ex = W4A16Experts.from_gptq(w13_qweight[None], w13_qzeros[None], w13_scales[None],
+                                    w2_qweight[None], w2_qzeros[None], w2_scales[None],
+                                    group_size=group_size)
+        gw = gate_weight.reshape(-1)
+        _check_cuda("gate_weight", gw, torch.bfloat16, 1)
+        if gw.numel() != ex.hidden:
+            raise ValueError("gate_weight must have hidden entries")
+        return cls(ex.blobs[0], gw.contiguous())
+
+
+# ---------------------------------------------------------------------------
+# the layer
+# ---------------------------------------------------------------------------
+def layer_workspace(m: int, experts: W4A16Experts, top_k: int, device) -> torch.Tensor:
+    nbytes = _lib.layer_workspace_bytes(m, experts.num_experts, top_k, experts.hidden, experts.inter)
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | None,
+                    experts: W4A16Experts, top_k: int, renormalize: bool = True,
+                    shared: SharedExpert | None = None, *,
+                    topk_weights: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
+                    slot_table: torch.Tensor | None = None, slot_cache: torch.Tensor | None = None,
+                    host_store: torch.Tensor | None = None, zero_mode: str = "raw",
+                    out: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,
+                    topk_out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                    demand_log: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One W4A16 MoE layer forward: router (when ``router_logits`` is given,
+    else the given ``topk_weights``/``topk_ids``), align, gate_up + SiLU*up,
+    down + routed weight, top-k sum and the sigmoid-gated shared expert.
+
+    Weights: ``experts.blobs`` (slot = expert), or with ``slot_table`` [E]
+    int32 the slot cache ``slot_cache`` [S, bytes] (slot -1 = not resident,
+    read from the pinned ``host_store`` [E, bytes] through its device
+    mapping). Returns ``out`` [M, H] bf16."""
+    _check_cuda("hidden_states", hidden_states, torch.bfloat16, 2)
+    m, h = hidden_states.shape
+    if h != experts.hidden:
+        raise ValueError(f"hidden_states last dim {h} != experts hidden {experts.hidden}")
+    e = experts.num_experts
+    if router_logits is not None:
+        _check_cuda("router_logits", router_logits, torch.float32, 2)
+        if router_logits.shape != (m, e):
+            raise ValueError(f"router_logits must be {(m, e)}, got {tuple(router_logits.shape)}")
+    else:
+        if topk_weights is None or topk_ids is None:
+            raise ValueError("give router_logits or topk_weights and topk_ids")
+        _check_cuda("topk_weights", topk_weights, torch.float32, 2)
+        _check_cuda("topk_ids", topk_ids, torch.int32, 2)
+        if topk_weights.shape != (m, top_k) or topk_ids.shape != (m, top_k):
+            raise ValueError(f"topk_weights/topk_ids must be {(m, top_k)}")
+    if zero_mode not in ZERO_MODES:
+        raise ValueError(f"zero_mode must be one of {sorted(ZERO_MODES)}")
+    blobs = experts.blobs
+    if slot_table is not None:
+        _check_cuda("slot_table", slot_table, torch.int32, 1)
+        if slot_table.numel() != e:
+            raise ValueError("slot_table must have num_experts entries")
+        blobs = slot_cache
+        if slot_cache is None and host_store is None:
+            raise ValueError("slot_table needs slot_cache and/or host_store")
+    if blobs is not None:
+        _check_cuda("expert blobs", blobs, torch.uint8)
+    host_ptr = None
+    if host_store is not None:
+        if not host_store.is_pinned():
+            raise ValueError("host_store must be pinned host memory")
+        host_ptr = C.c_void_p(host_store.data_ptr())
+    dev = hidden_states.device
+    if out is None:
+        out = torch.empty((m, h), dtype=torch.bfloat16, device=dev)
+    _check_cuda("out", out, torch.bfloat16, 2)
+    _check_cuda("out_f32", out_f32, torch.float32, 2)
+    if workspace is None:
+        workspace = layer_workspace(m, experts, top_k, dev)
+    args = _lib.MtpMoeLayerArgs()
+    args.num_tokens, args.hidden, args.inter, args.num_experts = m, h, experts.inter, e
+    args.top_k, args.group_size, args.renormalize = top_k, experts.group_size, int(bool(renormalize))
+    args.zero_mode = ZERO_MODES[zero_mode]
+    args.hidden_states = hidden_states.data_ptr()
+    args.router_logits = router_logits.data_ptr() if router_logits is not None else None
+    args.topk_weights = topk_weights.data_ptr() if topk_weights is not None else None
+    args.topk_ids = topk_ids.data_ptr() if topk_ids is not None else None
+    args.expert_blobs = blobs.data_ptr() if blobs is not None else None
+    args.expert_bytes = experts.expert_bytes
+    args.slot_table = slot_table.data_ptr() if slot_table is not None else None
+    args.host_blobs = host_ptr.value if host_ptr is not None else None
+    args.shared_blob = shared.blob.data_ptr() if shared is not None else None
+    args.shared_gate_weight = shared.gate_weight.data_ptr() if shared is not None else None
+    args.out = out.data_ptr()
+    args.out_f32 = out_f32.data_ptr() if out_f32 is not None else None
+    if topk_out is not None:
+        args.topk_weights_out = topk_out[0].data_ptr()
+        args.topk_ids_out = topk_out[1].data_ptr()
+    args.demand_log = demand_log.data_ptr() if demand_log is not None else None
+    args.status = status.data_ptr() if status is not None else None
+    args.workspace = workspace.data_ptr()
+    args.workspace_bytes = workspace.numel()
+    _lib.call("mtp_w4a16_moe_layer", C.byref(args), _stream(hidden_states))
+    return out
+
+
+def fused_experts(hidden_states: torch.Tensor, w1: W4A16Experts, w2=None,
+                  topk_weights: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
+                  inplace: bool = False, activation: str = "silu",
+                  apply_router_weight_on_input: bool = False, global_num_experts: int = -1,
+                  expert_map: torch.Tensor | None = None, quant_config=None, *,
+                  shared: SharedExpert | None = None, zero_mode: str = "raw") -> torch.Tensor:
+    """vLLM ``fused_experts`` shape: routed experts given by ``topk_weights`` /
+    ``topk_ids``. ``w1`` carries both projections (the kernel-layout blob holds
+    w13 and w2 together), so ``w2`` must be None or the same object."""
+    if w2 is not None and w2 is not w1:
+        raise ValueError("w2 must be None or the same W4A16Experts as w1 (one blob per expert)")
+    if activation.lower() != "silu":
+        raise ValueError(f"only SiLU is supported, got {activation!r}")
+    if apply_router_weight_on_input:
+        raise ValueError("apply_router_weight_on_input is not supported")
+    if expert_map is not None:
+        raise ValueError("use slot_table / expert-parallel entry points for expert_map")
+    if global_num_experts not in (-1, w1.num_experts):
+        raise ValueError("global_num_experts must equal the experts' count")
+    if topk_ids is not None and topk_ids.dtype != torch.int32:
+        topk_ids = topk_ids.to(torch.int32)
+    if topk_weights is not None and topk_weights.dtype != torch.float32:
+        topk_weights = topk_weights.to(torch.float32)
+    out = moe_layer_w4a16(hidden_states, None, w1, int(topk_ids.shape[1]), shared=shared,
+                          topk_weights=topk_weights.contiguous(), topk_ids=topk_ids.contiguous(),
+                          zero_mode=zero_mode)
+    if inplace:
+        # The layer reads hidden_states until its last kernel, so the result is
+        # written to a separate buffer first.
+        hidden_states.copy_(out)
+        return hidden_states
+    return out

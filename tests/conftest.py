@@ -1,0 +1,41 @@
+"""Shared pytest setup: repo root on sys.path, the ``gpu`` marker, fixtures."""
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+GOLDEN = ROOT / "tests" / "golden"
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (run on a B200 with -m gpu)")
+
+
+@pytest.fixture(scope="session")
+def built_lib():
+    """The in-tree C-ABI library (built here if missing or stale; nvcc cross-compiles)."""
+    from mtp_b200 import build as b
+    if b.LIB.exists():
+        try:
+            return b.build(quiet=True)
+        except Exception:
+            return b.LIB
+    return b.build(quiet=True)
+
+
+@pytest.fixture(scope="session")
+def cuda_device(built_lib):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test selected but no CUDA device is visible")
+    import mtp_b200
+    mtp_b200.load_library()
+    return torch.device("cuda:0")
+
+
+def golden(name: str):
+    import torch
+    return torch.load(GOLDEN / name, weights_only=False)
