@@ -74,6 +74,10 @@ enum MtpStatus {
 MTP_API const char* mtp_status_string(int status);
 MTP_API int mtp_abi_version(void);
 
+/* Device address of pinned (page-locked, mapped) host memory, for
+ * MtpMoeLayerArgs.host_blobs: cudaHostGetDevicePointer on the current device. */
+MTP_API int mtp_host_device_pointer(const void* host_ptr, void** device_ptr);
+
 /* ---- router (softmax -> top-k -> renormalise) ----------------------------- */
 /* logits [M, E] fp32 -> topk_weights [M, k] fp32, topk_ids [M, k] int32
  * (descending; exact ties -> lower expert id), token_expert_indices [M, k]

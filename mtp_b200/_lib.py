@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmtp_b200.so"
 EXPORTS = (
     "mtp_status_string",
     "mtp_abi_version",
+    "mtp_host_device_pointer",
     "mtp_router_topk",
     "mtp_moe_align_sizes",
     "mtp_moe_align",
@@ -55,6 +56,7 @@ class MtpMoeLayerArgs(C.Structure):
 _SIGS = {
     "mtp_status_string": (C.c_char_p, [C.c_int]),
     "mtp_abi_version": (C.c_int, []),
+    "mtp_host_device_pointer": (C.c_int, [vp, C.POINTER(vp)]),
     "mtp_router_topk": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, vp, vp]),
     "mtp_moe_align_sizes": (C.c_int, [i32, i32, i32, i32, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
     "mtp_moe_align": (C.c_int, [vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp, vp, vp]),
@@ -118,3 +120,10 @@ def layer_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> in
     out = i64()
     call("mtp_w4a16_moe_layer_workspace_size", m, e, k, hidden, inter, C.byref(out))
     return out.value
+
+
+def host_device_pointer(host_ptr: int) -> int:
+    """Device address of a pinned host buffer (cudaHostGetDevicePointer)."""
+    out = vp()
+    call("mtp_host_device_pointer", vp(host_ptr), C.byref(out))
+    return int(out.value)

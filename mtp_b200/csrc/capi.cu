@@ -25,13 +25,16 @@ static AlignSizes align_sizes(int numel, int E, int BM, int pad) {
 
 // Workspace of the layer call, each region 256-byte aligned.
 struct LayerWs {
-  int64_t tw, tid, sorted, eids, ntpp, segs, nseg, hbuf, ybuf, total;
+  int64_t tw, tid, sorted, eids, ntpp, segs, nseg, gate, wseg, nws, seg_done, done, status, hbuf, ybuf,
+      total;
+  int max_ws;
 };
 
 static LayerWs layer_ws(int M, int E, int k, int H, int I) {
   const int numel = M * k;
   const AlignSizes s = align_sizes(numel, E, kLayerBM, 0);
   LayerWs w;
+  w.max_ws = fused_max_work_segments(M, s.max_seg, s.max_blocks);
   int64_t o = 0;
   auto take = [&](int64_t bytes) {
     const int64_t at = o;
@@ -45,6 +48,12 @@ static LayerWs layer_ws(int M, int E, int k, int H, int I) {
   w.ntpp = take(4);
   w.segs = take(12LL * s.max_seg);
   w.nseg = take(4);
+  w.gate = take(4LL * M);
+  w.wseg = take(4LL * kWsInts * w.max_ws);
+  w.nws = take(4);
+  w.seg_done = take(4LL * w.max_ws);
+  w.done = take(4);
+  w.status = take(16);
   w.hbuf = take(2LL * (numel + M) * I);
   w.ybuf = take(4LL * (numel + M) * H);
   w.total = o;
@@ -75,6 +84,18 @@ const char* mtp_status_string(int status) {
 
 int mtp_abi_version(void) { return 1; }
 
+int mtp_host_device_pointer(const void* host_ptr, void** device_ptr) {
+  if (!host_ptr || !device_ptr) return MTP_ERR_NULL;
+  *device_ptr = nullptr;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, const_cast<void*>(host_ptr), 0) != cudaSuccess) {
+    cudaGetLastError();
+    return MTP_ERR_CUDA;
+  }
+  *device_ptr = d;
+  return MTP_OK;
+}
+
 int mtp_router_topk(const float* logits, int32_t M, int32_t E, int32_t k, int32_t renormalize,
                     float* topk_weights, int32_t* topk_ids, int32_t* token_expert_indices,
                     void* stream) {
@@ -101,12 +122,14 @@ int mtp_moe_align(const int32_t* topk_ids, int32_t numel, int32_t num_experts, i
                   const int32_t* expert_map, int32_t ignore_invalid_experts, int32_t pad_sorted_ids,
                   int32_t* sorted_token_ids, int32_t* expert_ids, int32_t* num_tokens_post_padded,
                   int32_t* segments, int32_t* num_segments, void* stream) {
-  if (!sorted_token_ids || !expert_ids || !num_tokens_post_padded) return MTP_ERR_NULL;
-  if (numel > 0 && !topk_ids) return MTP_ERR_NULL;
-  if ((segments == nullptr) != (num_segments == nullptr)) return MTP_ERR_NULL;
   if (numel < 0 || num_experts < 1 || num_experts > 1024 || block_size < 1 || block_size > 1024)
     return MTP_ERR_SHAPE;
   const AlignSizes s = align_sizes(numel, num_experts, block_size, pad_sorted_ids);
+  if (!num_tokens_post_padded) return MTP_ERR_NULL;
+  if ((s.cap > 0 && !sorted_token_ids) || (s.max_blocks > 0 && !expert_ids)) return MTP_ERR_NULL;
+  if (numel > 0 && !topk_ids) return MTP_ERR_NULL;
+  if ((segments == nullptr) != (num_segments == nullptr)) return MTP_ERR_NULL;
+  if (segments && s.max_seg > 0 && !segments) return MTP_ERR_NULL;
   return launch_moe_align(topk_ids, numel, num_experts, block_size, expert_map,
                           ignore_invalid_experts ? 1 : 0, s.cap, s.max_blocks, s.max_seg,
                           sorted_token_ids, expert_ids, num_tokens_post_padded, segments,
@@ -189,6 +212,55 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   const int numel = M * k;
   const AlignSizes s = align_sizes(numel, E, kLayerBM, 0);
 
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
+  int32_t* eids = reinterpret_cast<int32_t*>(ws + w.eids);
+  int32_t* ntpp = reinterpret_cast<int32_t*>(ws + w.ntpp);
+  int32_t* segs = reinterpret_cast<int32_t*>(ws + w.segs);
+  int32_t* nseg = reinterpret_cast<int32_t*>(ws + w.nseg);
+
+  if (fused_supported(H, I, G)) {
+    int32_t* status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
+    RouteArgs r;
+    r.M = M; r.H = H; r.E = E; r.k = k; r.renorm = a.renormalize ? 1 : 0;
+    r.has_shared = a.shared_blob ? 1 : 0;
+    r.numel = numel; r.cap = s.cap; r.max_blocks = s.max_blocks; r.max_seg = s.max_seg;
+    r.max_ws = w.max_ws;
+    r.logits = a.router_logits;
+    r.x = a.hidden_states;
+    r.gate_w = a.shared_gate_weight;
+    if (a.router_logits) {
+      r.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
+      r.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
+    } else {
+      r.topk_w = const_cast<float*>(a.topk_weights);
+      r.topk_ids = const_cast<int32_t*>(a.topk_ids);
+    }
+    r.gate = reinterpret_cast<float*>(ws + w.gate);
+    r.sorted = sorted; r.eids = eids; r.ntpp = ntpp; r.segs = segs; r.nseg = nseg;
+    r.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
+    r.nws = reinterpret_cast<int32_t*>(ws + w.nws);
+    r.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);
+    r.done = reinterpret_cast<int32_t*>(ws + w.done);
+    r.blobs = a.expert_blobs; r.expert_bytes = a.expert_bytes;
+    r.slot_table = a.slot_table; r.host_blobs = a.host_blobs; r.shared_blob = a.shared_blob;
+    r.status = status;
+    r.demand_log = a.demand_log;
+
+    FusedArgs f;
+    f.M = M; f.H = H; f.I = I; f.E = E; f.k = k; f.numel = numel; f.zero_mode = a.zero_mode;
+    f.has_shared = r.has_shared; f.G = G;
+    f.x = a.hidden_states; f.topk_w = r.topk_w; f.topk_ids = r.topk_ids;
+    f.wseg = r.wseg; f.nws = r.nws;
+    f.L = L;
+    f.gate = r.gate; f.seg_done = r.seg_done; f.done = r.done;
+    f.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
+    f.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
+    f.out = a.out; f.out_f32 = a.out_f32;
+    f.status = status;
+    f.stages = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
+    return launch_moe_fused(f, r, st);
+  }
+
   const float* tw = a.topk_weights;
   const int32_t* tid = a.topk_ids;
   if (a.router_logits) {
@@ -200,11 +272,6 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
     tw = w_out;
     tid = i_out;
   }
-  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
-  int32_t* eids = reinterpret_cast<int32_t*>(ws + w.eids);
-  int32_t* ntpp = reinterpret_cast<int32_t*>(ws + w.ntpp);
-  int32_t* segs = reinterpret_cast<int32_t*>(ws + w.segs);
-  int32_t* nseg = reinterpret_cast<int32_t*>(ws + w.nseg);
   int r = launch_moe_align(tid, numel, E, kLayerBM, nullptr, 0, s.cap, s.max_blocks, s.max_seg,
                            sorted, eids, ntpp, segs, nseg, st);
   if (r != MTP_OK) return r;

@@ -25,6 +25,65 @@ struct MoeDevArgs {
   int32_t* status;            // [4] or NULL
 };
 
+// Work segment: kWsBlocks token block(s) of one expert (or of the shared
+// expert), written by the route kernel and copied into shared memory by the
+// fused kernel. 12 ints = 48 bytes (16-byte multiple). One block per segment
+// lets every unit of a segment reuse the same operand rows.
+constexpr int kWsBlocks = 1;
+constexpr int kWsInts = 4 + 8 * kWsBlocks;
+//   [0..1] expert blob address (0 = missing), [2] block count,
+//   [3] flags (bit 0 shared expert, bit 1 blob in host memory),
+//   [4..] pair ids (row of h / y), -1 for padding.
+
+// Device-side arguments of the fused layer kernel (moe_fused.cu).
+struct FusedArgs {
+  int M, H, I, E, k, numel, zero_mode, has_shared, G;
+  const uint16_t* x;
+  const float* topk_w;
+  const int32_t* topk_ids;
+  const int32_t* wseg;       // [max_ws][kWsInts]
+  const int32_t* nws;        // [1]
+  MtpExpertLayout L;
+  const float* gate;         // [M] sigmoid(x . w_g)
+  int32_t* seg_done;         // [max_ws] W1 units published per work segment
+  int32_t* done;             // [1] CTAs finished with W2
+  uint16_t* hbuf;
+  float* ybuf;
+  uint16_t* out;
+  float* out_f32;
+  int32_t* status;
+  int stages;
+  uint32_t stage_bytes;
+  uint32_t xbuf_bytes;
+};
+
+// Arguments of the route kernel that precedes it.
+struct RouteArgs {
+  int M, H, E, k, renorm, has_shared, numel, cap, max_blocks, max_seg, max_ws;
+  const float* logits;       // or NULL (use the given topk_w / topk_ids)
+  const uint16_t* x;
+  const uint16_t* gate_w;
+  float* topk_w;
+  int32_t* topk_ids;
+  float* gate;
+  int32_t* sorted;
+  int32_t* eids;
+  int32_t* ntpp;
+  int32_t* segs;
+  int32_t* nseg;
+  int32_t* wseg;
+  int32_t* nws;
+  int32_t* seg_done;
+  int32_t* done;
+  const uint8_t* blobs;
+  int64_t expert_bytes;
+  const int32_t* slot_table;
+  const uint8_t* host_blobs;
+  const uint8_t* shared_blob;
+  int32_t* status;
+  int32_t* demand_log;
+};
+
 int launch_router_topk(const float* logits, int M, int E, int k, int renorm, float* w,
                        int32_t* ids, int32_t* tei, cudaStream_t st);
 int launch_moe_align(const int32_t* ids, int numel, int E, int BM, const int32_t* emap,
@@ -38,5 +97,9 @@ int gptq_dequant(const int32_t* q, const int32_t* z, const uint16_t* s, const in
                  int N, int G, int zero_mode, float* out, cudaStream_t st);
 int launch_moe_decode(const MoeDevArgs& a, int G, const uint16_t* gate_w, uint16_t* out,
                       float* out_f32, int32_t* demand_log, cudaStream_t st);
+
+bool fused_supported(int H, int I, int G);
+int fused_max_work_segments(int M, int max_seg, int max_blocks);
+int launch_moe_fused(const FusedArgs& a, const RouteArgs& r, cudaStream_t st);
 
 }  // namespace mtp

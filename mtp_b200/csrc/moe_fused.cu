@@ -1,0 +1,884 @@
+// The W4A16 MoE layer forward on sm_100a as two kernels:
+//
+//   route  (1 CTA, 1024 threads): router softmax/top-k/renormalise, the shared
+//          expert's sigmoid gate, moe_align (block 8), and the work-segment
+//          table the fused kernel runs on: each entry is one token block of
+//          one expert with its blob address already resolved through the slot
+//          table and its 8 pair ids inline. Resets the fused kernel's
+//          counters. Triggers programmatic dependent launch first thing so the
+//          fused kernel's CTAs are resident and waiting when it ends.
+//
+//   fused  (persistent: one CTA per SM, 18 warps, warp-specialised):
+//          warp 16  weight producer - streams each work unit's packed int4
+//                   strips, fp16 scales and zero nibbles from HBM into a ring
+//                   of shared-memory stages with 1-D bulk copies
+//                   (cp.async.bulk completing on an mbarrier), running ahead
+//                   of the consumers by the ring depth;
+//          warp 17  operand producer - brings the B operand of every token
+//                   block (8 x rows for W1, 8 h rows for W2) into a double
+//                   buffer; before the first W2 unit of a segment it waits
+//                   until all W1 units of that segment have published h;
+//          warps 0-15 consumers - dequantise int4 in registers (exponent
+//                   bias, exact q - z in bf16), m16n8k16 bf16 MMA with fp32
+//                   accumulation, per-chunk fp32 scale fold, cross-warp
+//                   reduction, then the epilogue.
+//
+// Work units, in this order (each CTA takes a contiguous range of each list;
+// a work segment is one token block, so ranges balance and every unit of a
+// segment reuses the same operand rows):
+//   W1 unit (segment, strip pair i): gate rows 16i..16i+15 and up rows
+//      I+16i..I+16i+15 over all of K = H -> h = silu(gate) * up (bf16) for
+//      every (token, slot) pair of the segment (vLLM fused_moe W1 +
+//      silu_and_mul, tracing/vllm_router_trace.py:19674-19719).
+//   W2 unit (segment, row octet r): down rows 128r..128r+127 over K = I ->
+//      y = h . W2^T times the router weight (MUL_ROUTED_WEIGHT, :19761-19782),
+//      fp32 per pair.
+// Then one grid-wide arrival; after the last CTA arrives every CTA combines a
+// slice of the output: out = sum over the top-k slots in slot order of y +
+// sigmoid(x . w_g) * y_shared (moe_sum :19801 and the shared-expert gate
+// :3994-4031, :4140-4152), so the result is deterministic.
+//
+// Consecutive units of the same single-block segment reuse the operand buffer
+// (the same x or h rows) without a new copy.
+//
+// Cross-CTA dependencies go through release/acquire counters. Units never
+// wait on later units and the final barrier is reached by every CTA after
+// its own units, so with all CTAs resident (one per SM, sized by shared
+// memory) nothing deadlocks. Every wait is bounded by a deadline on the
+// global timer; on expiry the kernel records bit 1 in status[2] and carries
+// on, so it always terminates.
+#include "internal.cuh"
+#include "route.cuh"
+
+namespace mtp {
+
+constexpr int kFBM = 8;            // tokens (pairs) per block = MMA N
+constexpr int kCW = 16;            // consumer warps
+constexpr int kCT = kCW * 32;      // consumer threads
+constexpr int kFusedThreads = kCT + 64;
+constexpr int kWProd = kCW;        // weight producer warp
+constexpr int kBProd = kCW + 1;    // operand producer warp
+constexpr int kMaxStages = 4;
+constexpr int kCtrlBytes = 512;
+constexpr int kWsCache = 64;       // work segments cached in shared memory per pass
+constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
+constexpr int kRedBytes = kCW * 2 * 4 * 32 * 4 + 2 * 4 * 32 * 4;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per layer call
+constexpr int kBarConsumers = 1;   // named barrier id for the consumer warps
+
+// ---------------------------------------------------------------------------
+// shared-memory control block and the per-pass work-segment view
+// ---------------------------------------------------------------------------
+struct Ctrl {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t xfull[2];
+  uint64_t xempty[2];
+  int stage_valid[kMaxStages];
+  int seg_first[2];   // first work segment of the pass range
+  int cached[2];      // 1 if the pass range's segments are in the table
+};
+static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
+
+struct Pass {
+  int ub, ue, per;    // unit range and units per segment
+  int seg_first;
+  const int* table;   // smem copy of segments [seg_first, ...] or the global table
+};
+
+__device__ __forceinline__ const int* ws_entry(const Pass& P, int seg) {
+  return P.table + static_cast<size_t>(seg - P.seg_first) * kWsInts;
+}
+
+__device__ __forceinline__ const uint8_t* ws_blob(const int* e) {
+  const uint64_t lo = static_cast<uint32_t>(e[0]), hi = static_cast<uint32_t>(e[1]);
+  return reinterpret_cast<const uint8_t*>((hi << 32) | lo);
+}
+
+__device__ __forceinline__ int pair_token(const FusedArgs& a, int p) {
+  return p >= a.numel ? p - a.numel : p / a.k;
+}
+
+__device__ __forceinline__ void unit_range(int total_units, int& b, int& e) {
+  const int64_t g = gridDim.x, c = blockIdx.x;
+  b = static_cast<int>(total_units * c / g);
+  e = static_cast<int>(total_units * (c + 1) / g);
+}
+
+__device__ __forceinline__ Pass make_pass(const FusedArgs& a, const Ctrl& cb, const int* table, int pass) {
+  Pass P;
+  const int S = *a.nws;
+  P.per = pass == 0 ? a.I / 16 : a.H / 128;
+  unit_range(S * P.per, P.ub, P.ue);
+  P.seg_first = cb.seg_first[pass];
+  P.table = cb.cached[pass] ? table + pass * kWsCache * kWsInts : a.wseg + static_cast<size_t>(P.seg_first) * kWsInts;
+  return P;
+}
+
+// A unit reuses the operand buffer of the previous unit when both belong to
+// the same single-block segment (same rows).
+__device__ __forceinline__ bool reuses_operand(const Pass& P, int u) {
+  if (u == P.ub) return false;
+  const int s = u / P.per;
+  return s == (u - 1) / P.per && ws_entry(P, s)[2] == 1;
+}
+
+__device__ __forceinline__ void record_timeout(const FusedArgs& a) { atomicOr(a.status + 2, 1); }
+
+__device__ __forceinline__ uint32_t lds8(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+// Byte ranges of a unit inside the expert blob and inside the stage.
+struct Piece {
+  uint32_t src_off;
+  uint32_t dst_off;
+  uint32_t bytes;
+};
+
+__device__ __forceinline__ int w1_pieces(const FusedArgs& a, int strip, Piece* p) {
+  const uint32_t sb = 8u * a.H;  // one 16-row strip over K = H
+  const uint32_t scb = static_cast<uint32_t>(a.H / a.G) * 32u;
+  const uint32_t zpb = static_cast<uint32_t>(a.H / a.G) * 8u;
+  const uint32_t up = a.I / 16 + strip;
+  const uint32_t L13 = static_cast<uint32_t>(a.L.w13_qweight), S13 = static_cast<uint32_t>(a.L.w13_scales),
+                 Z13 = static_cast<uint32_t>(a.L.w13_zeros);
+  p[0] = {L13 + strip * sb, 0, sb};
+  p[1] = {L13 + up * sb, sb, sb};
+  p[2] = {S13 + strip * scb, 2 * sb, scb};
+  p[3] = {S13 + up * scb, 2 * sb + scb, scb};
+  p[4] = {Z13 + strip * zpb, 2 * sb + 2 * scb, zpb};
+  p[5] = {Z13 + up * zpb, 2 * sb + 2 * scb + zpb, zpb};
+  return 6;
+}
+
+__device__ __forceinline__ int w2_pieces(const FusedArgs& a, int octet, Piece* p) {
+  const uint32_t ob = 64u * a.I;  // 8 strips of 16 rows over K = I
+  const uint32_t scb = 8u * static_cast<uint32_t>(a.I / a.G) * 32u;
+  const uint32_t zpb = 8u * static_cast<uint32_t>(a.I / a.G) * 8u;
+  const uint32_t L2 = static_cast<uint32_t>(a.L.w2_qweight), S2 = static_cast<uint32_t>(a.L.w2_scales),
+                 Z2 = static_cast<uint32_t>(a.L.w2_zeros);
+  p[0] = {L2 + octet * ob, 0, ob};
+  p[1] = {S2 + octet * scb, ob, scb};
+  p[2] = {Z2 + octet * zpb, ob + scb, zpb};
+  return 3;
+}
+
+// ---------------------------------------------------------------------------
+// producers
+// ---------------------------------------------------------------------------
+__device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages,
+                                uint64_t deadline) {
+  const int lane = threadIdx.x & 31;
+  int st = 0;
+  uint32_t ph = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const Pass P = make_pass(a, cb, table, pass);
+    for (int u = P.ub; u < P.ue; ++u) {
+      const int seg = u / P.per, idx = u % P.per;
+      const int* e = ws_entry(P, seg);
+      const uint8_t* blob = ws_blob(e);
+      const bool host = (e[3] & 2) != 0;
+      Piece pc[6];
+      const int n = pass == 0 ? w1_pieces(a, idx, pc) : w2_pieces(a, idx, pc);
+      if (!mbar_wait(smem_u32(&cb.empty[st]), ph ^ 1u, deadline) && lane == 0) record_timeout(a);
+      uint8_t* dst = stages + static_cast<size_t>(st) * a.stage_bytes;
+      const uint32_t full = smem_u32(&cb.full[st]);
+      if (lane == 0) cb.stage_valid[st] = blob != nullptr;
+      if (blob != nullptr && !host) {
+        if (lane == 0) {
+          uint32_t total = 0;
+          for (int i = 0; i < n; ++i) total += pc[i].bytes;
+          mbar_arrive_expect_tx(full, total);
+          for (int i = 0; i < n; ++i) bulk_g2s(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full);
+        }
+      } else {
+        // Pinned host memory (demand fetch over the host link): a warp copy
+        // with eight 16-byte loads in flight per lane.
+        if (blob != nullptr) {
+          for (int i = 0; i < n; ++i) {
+            const uint8_t* src = blob + pc[i].src_off;
+            uint8_t* d = dst + pc[i].dst_off;
+            for (uint32_t o = lane * 16u; o < pc[i].bytes; o += 32u * 16u * 8u) {
+              uint4 v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t oo = o + j * 512u;
+                if (oo < pc[i].bytes) v[j] = ldg_stream16(src + oo);
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t oo = o + j * 512u;
+                if (oo < pc[i].bytes) *reinterpret_cast<uint4*>(d + oo) = v[j];
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full);
+      }
+      if (++st == a.stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+}
+
+__device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs,
+                                 uint64_t deadline) {
+  const int lane = threadIdx.x & 31;
+  int xb = 0;
+  uint32_t xph = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const Pass P = make_pass(a, cb, table, pass);
+    const uint32_t row_bytes = pass == 0 ? 2u * a.H : 2u * a.I;
+    const uint32_t row_stride = row_bytes + 16u;
+    int waited_seg = -1;
+    for (int u = P.ub; u < P.ue; ++u) {
+      const int seg = u / P.per;
+      if (reuses_operand(P, u)) continue;
+      const int* e = ws_entry(P, seg);
+      const int nb = e[2];
+      if (pass == 1 && seg != waited_seg) {
+        // every W1 unit of this segment has published its h columns
+        if (lane == 0) {
+          bool ok = true;
+          while (ld_acquire_gpu(a.seg_done + seg) < a.I / 16) {
+            if (global_timer_ns() > deadline) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) record_timeout(a);
+          fence_proxy_async_global();
+        }
+        __syncwarp();
+        waited_seg = seg;
+      }
+      for (int blk = 0; blk < nb; ++blk) {
+        if (!mbar_wait(smem_u32(&cb.xempty[xb]), xph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        const int p = lane < kFBM ? e[4 + blk * kFBM + lane] : -1;
+        const unsigned valid = __ballot_sync(kFullMask, p >= 0);
+        const uint32_t xfull = smem_u32(&cb.xfull[xb]);
+        if (lane == 0) mbar_arrive_expect_tx(xfull, __popc(valid) * row_bytes);
+        __syncwarp();
+        if (p >= 0) {
+          const uint8_t* src = pass == 0
+                                   ? reinterpret_cast<const uint8_t*>(a.x + static_cast<int64_t>(pair_token(a, p)) * a.H)
+                                   : reinterpret_cast<const uint8_t*>(a.hbuf + static_cast<int64_t>(p) * a.I);
+          bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
+        }
+        if (++xb == 2) {
+          xb = 0;
+          xph ^= 1u;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// consumers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void zero_bias_from_byte(uint32_t zb, int zero_mode, uint32_t& lo, uint32_t& hi) {
+  if (zero_mode == MTP_ZERO_SYM8) {
+    lo = hi = zero_bias_pair(8);
+  } else {
+    lo = zero_bias_pair(zb & 0xF);
+    hi = zero_bias_pair(zb >> 4);
+  }
+}
+
+__device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ void fold(float (&acc)[4], const float (&d)[4], uint32_t scw) {
+  const float2 s = half2_bits_to_float2(scw);
+  acc[0] = fmaf(s.x, d[0], acc[0]);
+  acc[1] = fmaf(s.x, d[1], acc[1]);
+  acc[2] = fmaf(s.y, d[2], acc[2]);
+  acc[3] = fmaf(s.y, d[3], acc[3]);
+}
+
+template <int W1C, int W2C>
+__device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages, uint8_t* xbufs,
+                          float* red, uint64_t deadline) {
+  const int ctid = threadIdx.x;  // 0..511
+  const int warp = ctid >> 5, lane = ctid & 31, g = lane >> 2, t = lane & 3;
+  const int nkw = a.H / 64 / W1C;  // warps along K in W1 (<= 16)
+  int st = 0, xb = 0;
+  uint32_t ph = 0, xph = 0;
+  const int ld_row = lane & 7, ld_mat = lane >> 3;  // ldmatrix row address of this lane
+
+  for (int pass = 0; pass < 2; ++pass) {
+    const Pass P = make_pass(a, cb, table, pass);
+    for (int u = P.ub; u < P.ue; ++u) {
+      const int seg = u / P.per, idx = u % P.per;
+      const int* e = ws_entry(P, seg);
+      const int nb = e[2];
+      const bool reuse = reuses_operand(P, u);
+      const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
+      if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && ctid == 0) record_timeout(a);
+      const bool wvalid = cb.stage_valid[st] != 0;
+      const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
+      for (int blk = 0; blk < nb; ++blk) {
+        if (!reuse && !mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && ctid == 0) record_timeout(a);
+        const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
+        const int* cols = e + 4 + blk * kFBM;
+        if (pass == 0) {
+          // ------------------------------ W1 ------------------------------
+          const uint32_t rs = 2u * a.H + 16u;
+          float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+          if (wvalid && warp < nkw) {
+            const uint32_t sb = 8u * a.H, scb = (a.H / a.G) * 32u, zpb = (a.H / a.G) * 8u;
+            // all operands of the warp's W1C chunks x 2 strips first, then the
+            // MMAs interleaved over 2*W1C independent accumulators
+            uint4 w[W1C][2];
+            uint32_t bf[W1C][8];
+            uint32_t zlo[W1C][2], zhi[W1C][2], scw[W1C][2];
+#pragma unroll
+            for (int j = 0; j < W1C; ++j) {
+              const int c = warp * W1C + j;
+              const int grp = c * 64 / a.G;
+              const uint32_t xa = xbase + ld_row * rs + (64 * c + 8 * ld_mat) * 2;
+              ldsm_x4(xa, bf[j][0], bf[j][1], bf[j][2], bf[j][3]);
+              ldsm_x4(xa + 64, bf[j][4], bf[j][5], bf[j][6], bf[j][7]);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                w[j][q] = lds128(sbase + q * sb + (c * 32 + lane) * 16);
+                scw[j][q] = lds32(sbase + 2 * sb + q * scb + (grp * 8 + g) * 4);
+                const uint32_t zb =
+                    a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 2 * sb + 2 * scb + q * zpb + grp * 8 + g) : 0x88u;
+                zero_bias_from_byte(zb, a.zero_mode, zlo[j][q], zhi[j][q]);
+              }
+            }
+            float d[W1C][2][4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+              for (int j = 0; j < W1C; ++j)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  uint32_t A[4];
+                  dequant_word(pick(w[j][q], kk), zlo[j][q], zhi[j][q], A);
+                  if (kk == 0)
+                    mma_bf16_16816_zc(d[j][q], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+                  else
+                    mma_bf16_16816(d[j][q], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+                }
+#pragma unroll
+            for (int j = 0; j < W1C; ++j)
+#pragma unroll
+              for (int q = 0; q < 2; ++q) fold(acc[q], d[j][q], scw[j][q]);
+          }
+          if (!keep) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&cb.xempty[xb]));
+          }
+          if (warp < nkw) {
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) red[((warp * 2 + q) * 4 + r) * 32 + lane] = acc[q][r];
+          }
+          named_bar_sync(kBarConsumers, kCT);
+          {
+            // thread 4m+s: position m = (r, l) of the 16x8 tile, s = (strip,
+            // half of the K warps); halves summed, then gate/up met by shuffle
+            const int m = ctid >> 2, sub = ctid & 3, q = sub >> 1, half = sub & 1;
+            float v = 0.f;
+            for (int w = half; w < nkw; w += 2) v += red[w * 256 + q * 128 + m];
+            v += __shfl_xor_sync(kFullMask, v, 1);
+            const float up = __shfl_xor_sync(kFullMask, v, 2);
+            if (sub == 0) {
+              const int r = m >> 5, l = m & 31;
+              const int p = cols[2 * (l & 3) + (r & 1)];
+              if (p >= 0) {
+                const int row = (l >> 2) + 8 * (r >> 1);
+                a.hbuf[static_cast<int64_t>(p) * a.I + 16 * idx + row] =
+                    __bfloat16_as_ushort(__float2bfloat16(silu(v) * up));
+              }
+            }
+          }
+          // the barrier protects red from the next unit and orders the h stores
+          // before the release below
+          named_bar_sync(kBarConsumers, kCT);
+          if (blk == nb - 1 && ctid == 0) red_release_gpu_add(a.seg_done + seg, 1);
+        } else {
+          // ------------------------------ W2 ------------------------------
+          const uint32_t rs = 2u * a.I + 16u;
+          const int sidx = warp >> 1, hk = warp & 1;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          if (wvalid) {
+            const uint32_t sb = 8u * a.I;  // one strip over K = I
+            const uint32_t scb_all = 8u * (a.I / a.G) * 32u;
+            const int gper = a.I / a.G;
+            uint4 w[W2C];
+            uint32_t bf[W2C][8];
+            uint32_t zlo[W2C], zhi[W2C], scw[W2C];
+#pragma unroll
+            for (int j = 0; j < W2C; ++j) {
+              const int c = hk * W2C + j;
+              const int grp = c * 64 / a.G;
+              const uint32_t xa = xbase + ld_row * rs + (64 * c + 8 * ld_mat) * 2;
+              ldsm_x4(xa, bf[j][0], bf[j][1], bf[j][2], bf[j][3]);
+              ldsm_x4(xa + 64, bf[j][4], bf[j][5], bf[j][6], bf[j][7]);
+              w[j] = lds128(sbase + sidx * sb + (c * 32 + lane) * 16);
+              scw[j] = lds32(sbase + 8 * sb + ((sidx * gper + grp) * 8 + g) * 4);
+              const uint32_t zb =
+                  a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 8 * sb + scb_all + (sidx * gper + grp) * 8 + g) : 0x88u;
+              zero_bias_from_byte(zb, a.zero_mode, zlo[j], zhi[j]);
+            }
+            float d[W2C][4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+              for (int j = 0; j < W2C; ++j) {
+                uint32_t A[4];
+                dequant_word(pick(w[j], kk), zlo[j], zhi[j], A);
+                if (kk == 0)
+                  mma_bf16_16816_zc(d[j], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+                else
+                  mma_bf16_16816(d[j], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+              }
+#pragma unroll
+            for (int j = 0; j < W2C; ++j) fold(acc, d[j], scw[j]);
+          }
+          if (!keep) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&cb.xempty[xb]));
+          }
+          if (hk == 1) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) red[(sidx * 4 + r) * 32 + lane] = acc[r];
+          }
+          named_bar_sync(kBarConsumers, kCT);
+          if (hk == 0) {
+            const int p0 = cols[2 * t], p1 = cols[2 * t + 1];
+            const float w0 = (p0 >= 0 && p0 < a.numel) ? a.topk_w[p0] : 1.f;
+            const float w1 = (p1 >= 0 && p1 < a.numel) ? a.topk_w[p1] : 1.f;
+            const int nbase = 128 * idx + 16 * sidx;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const int p = (r & 1) ? p1 : p0;
+              if (p >= 0) {
+                const float y = (acc[r] + red[(sidx * 4 + r) * 32 + lane]) * ((r & 1) ? w1 : w0);
+                a.ybuf[static_cast<int64_t>(p) * a.H + nbase + g + 8 * (r >> 1)] = y;
+              }
+            }
+          }
+          named_bar_sync(kBarConsumers, kCT);
+        }
+        if (!keep) {
+          if (++xb == 2) {
+            xb = 0;
+            xph ^= 1u;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&cb.empty[st]));
+      if (++st == a.stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+
+  // ------------------------- grid arrival + combine -------------------------
+  named_bar_sync(kBarConsumers, kCT);
+  if (ctid == 0) {
+    red_release_gpu_add(a.done, 1);
+    bool ok = true;
+    while (ld_acquire_gpu(a.done) < static_cast<int>(gridDim.x)) {
+      if (global_timer_ns() > deadline) {
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) record_timeout(a);
+  }
+  named_bar_sync(kBarConsumers, kCT);
+  const int quads = a.H / 4;
+  const int64_t total = static_cast<int64_t>(a.M) * quads;
+  const int64_t b = total * blockIdx.x / gridDim.x, e = total * (blockIdx.x + 1) / gridDim.x;
+  for (int64_t i = b + ctid; i < e; i += kCT) {
+    const int tok = static_cast<int>(i / quads);
+    const int n = static_cast<int>(i % quads) * 4;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < a.k; ++j) {
+      const int pp = tok * a.k + j;
+      const int ex = a.topk_ids[pp];
+      if (ex >= 0 && ex < a.E) {
+        const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(pp) * a.H + n);
+        sum.x += y.x;
+        sum.y += y.y;
+        sum.z += y.z;
+        sum.w += y.w;
+      }
+    }
+    if (a.has_shared) {
+      const float gt = a.gate[tok];
+      const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(a.numel + tok) * a.H + n);
+      sum.x = fmaf(gt, y.x, sum.x);
+      sum.y = fmaf(gt, y.y, sum.y);
+      sum.z = fmaf(gt, y.z, sum.z);
+      sum.w = fmaf(gt, y.w, sum.w);
+    }
+    const int64_t o = static_cast<int64_t>(tok) * a.H + n;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(sum.x, sum.y);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(sum.z, sum.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(a.out + o) = packed;
+    if (a.out_f32) *reinterpret_cast<float4*>(a.out_f32 + o) = sum;
+  }
+}
+
+template <int W1C, int W2C>
+__global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
+  int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
+  uint8_t* stages = smem + kCtrlBytes + kTableBytes;
+  uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
+  float* red = reinterpret_cast<float*>(xbufs + 2 * a.xbuf_bytes);
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(smem_u32(&cb.full[i]), 1);
+      mbar_init(smem_u32(&cb.empty[i]), kCW);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&cb.xfull[i]), 1);
+      mbar_init(smem_u32(&cb.xempty[i]), kCW);
+    }
+    fence_mbar_init();
+  }
+  // Everything below reads what the route kernel wrote.
+  pdl_wait();
+  const uint64_t deadline = global_timer_ns() + kTimeoutNs;
+  // Copy this CTA's two ranges of work segments into shared memory.
+  {
+    const int S = *a.nws;
+    for (int pass = 0; pass < 2; ++pass) {
+      const int per = pass == 0 ? a.I / 16 : a.H / 128;
+      int ub, ue;
+      unit_range(S * per, ub, ue);
+      const int first = ub / per;
+      const int last = ue > ub ? (ue - 1) / per : first - 1;
+      const int n = last - first + 1;
+      if (threadIdx.x == 0) {
+        cb.seg_first[pass] = first;
+        cb.cached[pass] = n <= kWsCache;
+      }
+      if (n > 0 && n <= kWsCache) {
+        const int4* src = reinterpret_cast<const int4*>(a.wseg + static_cast<size_t>(first) * kWsInts);
+        int4* dst = reinterpret_cast<int4*>(table + pass * kWsCache * kWsInts);
+        for (int i = threadIdx.x; i < n * kWsInts / 4; i += kFusedThreads) dst[i] = src[i];
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == kWProd) {
+    weight_producer(a, cb, table, stages, deadline);
+  } else if (warp == kBProd) {
+    operand_producer(a, cb, table, xbufs, deadline);
+  } else {
+    consumers<W1C, W2C>(a, cb, table, stages, xbufs, red, deadline);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// route kernel
+// ---------------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(kAlignThreads) moe_route_kernel(RouteArgs r) {
+  pdl_launch_dependents();
+  extern __shared__ int sm[];
+  __shared__ int scan_tmp[32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) *r.done = 0;
+  for (int i = tid; i < r.max_ws; i += kAlignThreads) r.seg_done[i] = 0;
+  for (int tkn = warp; tkn < r.M; tkn += kAlignThreads / 32) {
+    if (r.logits) {
+      float w;
+      int id;
+      router_token<VPT>(r.logits + static_cast<int64_t>(tkn) * r.E, r.E, r.k, r.renorm, &w, &id);
+      if (lane < r.k) {
+        r.topk_w[tkn * r.k + lane] = w;
+        r.topk_ids[tkn * r.k + lane] = id;
+      }
+    }
+    if (r.has_shared) {
+      // sigmoid(x . w_g): 8 bf16 per 16-byte load, loads issued 2 at a time
+      // (the 1024-thread block leaves 64 registers a thread)
+      const uint4* xr = reinterpret_cast<const uint4*>(r.x + static_cast<int64_t>(tkn) * r.H);
+      const uint4* wg = reinterpret_cast<const uint4*>(r.gate_w);
+      float part = 0.f;
+      const int nvec = r.H / 8;
+      for (int v0 = lane; v0 < nvec; v0 += 32 * 2) {
+        uint4 xv[2], wv[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int v = v0 + 32 * j;
+          if (v < nvec) {
+            xv[j] = xr[v];
+            wv[j] = wg[v];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int v = v0 + 32 * j;
+          if (v < nvec) {
+            const uint32_t* xs = reinterpret_cast<const uint32_t*>(&xv[j]);
+            const uint32_t* ws = reinterpret_cast<const uint32_t*>(&wv[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              part = fmaf(__uint_as_float(xs[q] << 16), __uint_as_float(ws[q] << 16), part);
+              part = fmaf(__uint_as_float(xs[q] & 0xffff0000u), __uint_as_float(ws[q] & 0xffff0000u), part);
+            }
+          }
+        }
+      }
+      part = warp_sum(part);
+      if (lane == 0) r.gate[tkn] = 1.f / (1.f + expf(-part));
+    }
+  }
+  __syncthreads();
+  align_block(r.topk_ids, r.numel, r.E, kFBM, nullptr, 0, r.cap, r.max_blocks, r.max_seg, r.sorted, r.eids,
+              r.ntpp, r.segs, r.nseg, sm, scan_tmp);
+  __syncthreads();
+
+  // Work segments: the shared expert first, then each routed expert, every
+  // one cut into pieces of kWsBlocks token block(s).
+  const int nseg = *r.nseg;
+  const int shared_blocks = r.has_shared ? (r.M + kFBM - 1) / kFBM : 0;
+  const int shared_ws = (shared_blocks + kWsBlocks - 1) / kWsBlocks;
+  int mine = 0;  // work segments of routed segment tid
+  int e = -1, b0 = 0, nb = 0;
+  if (tid < nseg) {
+    e = r.segs[3 * tid];
+    b0 = r.segs[3 * tid + 1];
+    nb = r.segs[3 * tid + 2];
+    mine = (nb + kWsBlocks - 1) / kWsBlocks;
+  }
+  int total;
+  const int first = shared_ws + block_exclusive_scan(mine, &total, scan_tmp);
+  if (tid == 0) *r.nws = shared_ws + total;
+  // segment -> (first work segment, expert, blocks) for the warp-parallel fill
+  int* ws_first = sm;                 // [nseg] (align scratch is free now)
+  if (tid < nseg) ws_first[tid] = first;
+  if (tid < nseg) {
+    const int slot = r.slot_table ? r.slot_table[e] : e;
+    if (slot < 0) atomicAdd(r.host_blobs ? r.status + 0 : r.status + 1, 1);
+  }
+  __syncthreads();
+  const int nws = shared_ws + total;
+  for (int wsi = warp; wsi < nws; wsi += kAlignThreads / 32) {
+    int32_t* w = r.wseg + static_cast<size_t>(wsi) * kWsInts;
+    const uint8_t* blob = nullptr;
+    int flags = 0, cnt = 0, base = 0;
+    bool shared = wsi < shared_ws;
+    int seg = -1;
+    if (shared) {
+      blob = r.shared_blob;
+      flags = 1;
+      cnt = min(kWsBlocks, shared_blocks - wsi * kWsBlocks);
+      base = wsi * kWsBlocks * kFBM;  // first token
+    } else {
+      // the routed segment whose range holds wsi (ws_first ascending)
+      int lo = 0, hi = nseg - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (ws_first[mid] <= wsi) lo = mid; else hi = mid - 1;
+      }
+      seg = lo;
+      const int ex = r.segs[3 * seg], sb0 = r.segs[3 * seg + 1], snb = r.segs[3 * seg + 2];
+      const int q = wsi - ws_first[seg];
+      cnt = min(kWsBlocks, snb - q * kWsBlocks);
+      base = (sb0 + q * kWsBlocks) * kFBM;
+      const int slot = r.slot_table ? r.slot_table[ex] : ex;
+      if (slot >= 0) {
+        blob = r.blobs + static_cast<int64_t>(slot) * r.expert_bytes;
+      } else if (r.host_blobs) {
+        blob = r.host_blobs + static_cast<int64_t>(ex) * r.expert_bytes;
+        flags = 2;
+      }
+    }
+    if (lane < kWsBlocks * kFBM) {
+      int p = -1;
+      if (lane < cnt * kFBM) {
+        if (shared) {
+          const int tk = base + lane;
+          p = tk < r.M ? r.numel + tk : -1;
+        } else {
+          p = r.sorted[base + lane];
+          p = (p >= 0 && p < r.numel) ? p : -1;
+        }
+      }
+      w[4 + lane] = p;
+    }
+    if (lane == 0) {
+      const uint64_t addr = reinterpret_cast<uint64_t>(blob);
+      w[0] = static_cast<int32_t>(addr & 0xffffffffu);
+      w[1] = static_cast<int32_t>(addr >> 32);
+      w[2] = cnt;
+      w[3] = flags;
+    }
+  }
+  if (r.demand_log) {
+    if (tid == 0) r.demand_log[0] = nseg;
+    for (int i = tid; i < nseg; i += kAlignThreads) r.demand_log[1 + i] = r.segs[3 * i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct FusedGeometry {
+  int stages;
+  uint32_t stage_bytes, xbuf_bytes;
+  size_t smem;
+};
+
+static uint32_t round128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
+
+static FusedGeometry fused_geometry(int H, int I, int G) {
+  FusedGeometry f;
+  const uint64_t w1 = 16ull * H + 2ull * (H / G) * 32 + 2ull * (H / G) * 8;
+  const uint64_t w2 = 64ull * I + 8ull * (I / G) * 32 + 8ull * (I / G) * 8;
+  f.stage_bytes = round128(w1 > w2 ? w1 : w2);
+  const int maxrow = H > I ? H : I;
+  f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (2ull * maxrow + 16));
+  const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + kRedBytes;
+  const size_t budget = 227 * 1024;
+  int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
+  if (s > kMaxStages) s = kMaxStages;
+  f.stages = s;
+  f.smem = fixed + static_cast<size_t>(s) * f.stage_bytes;
+  return f;
+}
+
+static int device_sms() {
+  static int cached_dev = -1, cached_sms = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev != cached_dev) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cached_dev = dev;
+    cached_sms = n;
+  }
+  return cached_sms;
+}
+
+template <int W1C, int W2C>
+static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream_t st) {
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    if (cudaFuncSetAttribute(moe_fused_kernel<W1C, W2C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             227 * 1024) != cudaSuccess)
+      return MTP_ERR_CUDA;
+    configured = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(device_sms());
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = f.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, moe_fused_kernel<W1C, W2C>, a) != cudaSuccess) return MTP_ERR_LAUNCH;
+  return MTP_OK;
+}
+
+static bool fused_template(int H, int I, int* w1c, int* w2c) {
+  *w1c = H <= 1024 ? 1 : H / 1024;
+  *w2c = I / 128;
+  const bool w1ok = *w1c == 1 || *w1c == 2 || *w1c == 4;
+  const bool w2ok = *w2c == 1 || *w2c == 2 || *w2c == 4 || *w2c == 6 || *w2c == 8;
+  return w1ok && w2ok && H / 64 / *w1c <= kCW;
+}
+
+bool fused_supported(int H, int I, int G) {
+  if (G != 64 && G != 128) return false;
+  if (H % 128 || I % 128 || H % G || I % G) return false;
+  int w1c, w2c;
+  if (!fused_template(H, I, &w1c, &w2c)) return false;
+  return fused_geometry(H, I, G).stages >= 2;
+}
+
+int fused_max_work_segments(int M, int max_seg, int max_blocks) {
+  const int shared_blocks = (M + kFBM - 1) / kFBM;
+  return max_seg + max_blocks / kWsBlocks + (shared_blocks + kWsBlocks - 1) / kWsBlocks + 2;
+}
+
+int launch_moe_fused(const FusedArgs& a_in, const RouteArgs& r, cudaStream_t st) {
+  FusedArgs a = a_in;
+  const FusedGeometry f = fused_geometry(a.H, a.I, a.G);
+  a.stages = f.stages;
+  a.stage_bytes = f.stage_bytes;
+  a.xbuf_bytes = f.xbuf_bytes;
+  {
+    static int configured = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sm = static_cast<int>(align_smem_bytes(1024));
+    if (configured != dev) {
+      const bool ok =
+          cudaFuncSetAttribute(moe_route_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
+          cudaFuncSetAttribute(moe_route_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
+          cudaFuncSetAttribute(moe_route_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
+          cudaFuncSetAttribute(moe_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
+          cudaFuncSetAttribute(moe_route_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
+          cudaFuncSetAttribute(moe_route_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess;
+      if (!ok) return MTP_ERR_CUDA;
+      configured = dev;
+    }
+    const size_t smem = align_smem_bytes(r.E);
+    const int vpt = (r.E + 31) / 32;
+    if (vpt <= 1) moe_route_kernel<1><<<1, kAlignThreads, smem, st>>>(r);
+    else if (vpt <= 2) moe_route_kernel<2><<<1, kAlignThreads, smem, st>>>(r);
+    else if (vpt <= 4) moe_route_kernel<4><<<1, kAlignThreads, smem, st>>>(r);
+    else if (vpt <= 8) moe_route_kernel<8><<<1, kAlignThreads, smem, st>>>(r);
+    else if (vpt <= 16) moe_route_kernel<16><<<1, kAlignThreads, smem, st>>>(r);
+    else moe_route_kernel<32><<<1, kAlignThreads, smem, st>>>(r);
+    const int rs = launch_status();
+    if (rs != MTP_OK) return rs;
+  }
+  int w1c, w2c;
+  fused_template(a.H, a.I, &w1c, &w2c);
+#define MTP_FUSED_CASE(A, B) \
+  if (w1c == A && w2c == B) return launch_fused_t<A, B>(a, f, st);
+  MTP_FUSED_CASE(1, 1)
+  MTP_FUSED_CASE(1, 2)
+  MTP_FUSED_CASE(1, 4)
+  MTP_FUSED_CASE(2, 1)
+  MTP_FUSED_CASE(2, 2)
+  MTP_FUSED_CASE(2, 4)
+  MTP_FUSED_CASE(2, 6)
+  MTP_FUSED_CASE(2, 8)
+  MTP_FUSED_CASE(4, 4)
+  MTP_FUSED_CASE(4, 8)
+#undef MTP_FUSED_CASE
+  return MTP_ERR_SHAPE;
+}
+
+}  // namespace mtp

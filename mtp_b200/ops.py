@@ -170,7 +170,7 @@ class W4A16Experts:
         if w13_qzeros.shape != (e, hidden // group_size, two_i // 8) or w2_qzeros.shape != (e, inter // group_size, hidden // 8):
             raise ValueError("qzeros do not match group_size")
         layout = _lib.expert_layout(hidden, inter, group_size)
-        blobs = torch.empty((e, layout.bytes), dtype=torch.uint8, device=w13_qweight.device)
+        blobs = torch.zeros((e, layout.bytes), dtype=torch.uint8, device=w13_qweight.device)
         _lib.call("mtp_w4a16_repack_gptq", _p(w13_qweight), _p(w13_qzeros), _p(w13_scales.view(torch.int16)),
                   _p(w2_qweight), _p(w2_qzeros), _p(w2_scales.view(torch.int16)), e, hidden, inter,
                   group_size, _p(blobs), _stream(w13_qweight))
@@ -255,7 +255,7 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     if host_store is not None:
         if not host_store.is_pinned():
             raise ValueError("host_store must be pinned host memory")
-        host_ptr = C.c_void_p(host_store.data_ptr())
+        host_ptr = C.c_void_p(_lib.host_device_pointer(host_store.data_ptr()))
     dev = hidden_states.device
     if out is None:
         out = torch.empty((m, h), dtype=torch.bfloat16, device=dev)
