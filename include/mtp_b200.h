@@ -183,6 +183,22 @@ MTP_API int mtp_w4a16_moe_layer_workspace_size(int32_t num_tokens, int32_t num_e
                                        int32_t inter, int64_t* bytes);
 MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
 
+/* ---- the layer forward without a caller-provided workspace ------------------
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory (an FFI host that only passes pointers to buffers it
+ * was given; a serving loop whose device memory belongs to another allocator).
+ * Same arguments and results as mtp_w4a16_moe_layer, except that `workspace`
+ * and `workspace_bytes` are ignored: the scratch is a fixed array of
+ * MTP_NOALLOC_SCRATCH_BYTES compiled into the library (held by every GPU that
+ * loads it until exit), enough for M <= 48 at H = 2048, I = 512, E = 256,
+ * top-8. A request needing more returns MTP_ERR_WORKSPACE without launching.
+ * Allocates nothing. The first call on a device looks up the array's device
+ * address (with that device current), so make it before any stream capture.
+ * All calls share the array and it keeps the last call's contents; calls that
+ * overlap on the GPU race and must be serialised by the caller.            */
+#define MTP_NOALLOC_SCRATCH_BYTES (4u << 20)
+MTP_API int mtp_w4a16_moe_layer_noalloc(const MtpMoeLayerArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

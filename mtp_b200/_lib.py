@@ -26,6 +26,7 @@ EXPORTS = (
     "mtp_w4a16_repack_gptq",
     "mtp_w4a16_moe_layer_workspace_size",
     "mtp_w4a16_moe_layer",
+    "mtp_w4a16_moe_layer_noalloc",
 )
 
 MTP_ZERO_RAW = 0
@@ -65,6 +66,7 @@ _SIGS = {
     "mtp_w4a16_repack_gptq": (C.c_int, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp]),
     "mtp_w4a16_moe_layer_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_w4a16_moe_layer": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
+    "mtp_w4a16_moe_layer_noalloc": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
 }
 
 _lock = threading.Lock()
