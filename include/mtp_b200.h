@@ -143,8 +143,8 @@ MTP_API int mtp_w4a16_repack_gptq(const int32_t* w13_qweight, const int32_t* w13
 /* ---- the MoE layer forward ------------------------------------------------- */
 typedef struct MtpMoeLayerArgs {
   int32_t num_tokens;        /* M >= 1                                        */
-  int32_t hidden;            /* H: multiple of 256, <= 8192                   */
-  int32_t inter;             /* I: multiple of 64                             */
+  int32_t hidden;            /* H: multiple of 256, 256..2048                 */
+  int32_t inter;             /* I: multiple of 128, 128..1024                 */
   int32_t num_experts;       /* E: 1..1024 (global expert count)              */
   int32_t top_k;             /* 1..32                                         */
   int32_t group_size;        /* 64 or 128                                     */

@@ -188,7 +188,7 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   const int G = a.group_size;
   if (M < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return MTP_ERR_SHAPE;
   if (H < 256 || H > 2048 || H % 256) return MTP_ERR_SHAPE;
-  if (I < 64 || I > 1024 || I % 64) return MTP_ERR_SHAPE;
+  if (I < 128 || I > 1024 || I % 128) return MTP_ERR_SHAPE;
   if (G != 64 && G != 128) return MTP_ERR_SHAPE;
   if (I % G || H % G) return MTP_ERR_SHAPE;
   if (a.zero_mode != MTP_ZERO_RAW && a.zero_mode != MTP_ZERO_SYM8) return MTP_ERR_ARG;
@@ -218,76 +218,47 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   int32_t* segs = reinterpret_cast<int32_t*>(ws + w.segs);
   int32_t* nseg = reinterpret_cast<int32_t*>(ws + w.nseg);
 
-  if (fused_supported(H, I, G)) {
-    int32_t* status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
-    RouteArgs r;
-    r.M = M; r.H = H; r.E = E; r.k = k; r.renorm = a.renormalize ? 1 : 0;
-    r.has_shared = a.shared_blob ? 1 : 0;
-    r.numel = numel; r.cap = s.cap; r.max_blocks = s.max_blocks; r.max_seg = s.max_seg;
-    r.max_ws = w.max_ws;
-    r.logits = a.router_logits;
-    r.x = a.hidden_states;
-    r.gate_w = a.shared_gate_weight;
-    if (a.router_logits) {
-      r.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
-      r.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
-    } else {
-      r.topk_w = const_cast<float*>(a.topk_weights);
-      r.topk_ids = const_cast<int32_t*>(a.topk_ids);
-    }
-    r.gate = reinterpret_cast<float*>(ws + w.gate);
-    r.sorted = sorted; r.eids = eids; r.ntpp = ntpp; r.segs = segs; r.nseg = nseg;
-    r.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
-    r.nws = reinterpret_cast<int32_t*>(ws + w.nws);
-    r.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);
-    r.done = reinterpret_cast<int32_t*>(ws + w.done);
-    r.blobs = a.expert_blobs; r.expert_bytes = a.expert_bytes;
-    r.slot_table = a.slot_table; r.host_blobs = a.host_blobs; r.shared_blob = a.shared_blob;
-    r.status = status;
-    r.demand_log = a.demand_log;
-
-    FusedArgs f;
-    f.M = M; f.H = H; f.I = I; f.E = E; f.k = k; f.numel = numel; f.zero_mode = a.zero_mode;
-    f.has_shared = r.has_shared; f.G = G;
-    f.x = a.hidden_states; f.topk_w = r.topk_w; f.topk_ids = r.topk_ids;
-    f.wseg = r.wseg; f.nws = r.nws;
-    f.L = L;
-    f.gate = r.gate; f.seg_done = r.seg_done; f.done = r.done;
-    f.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
-    f.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
-    f.out = a.out; f.out_f32 = a.out_f32;
-    f.status = status;
-    f.stages = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
-    return launch_moe_fused(f, r, st);
-  }
-
-  const float* tw = a.topk_weights;
-  const int32_t* tid = a.topk_ids;
+  if (!fused_supported(H, I, G)) return MTP_ERR_SHAPE;
+  int32_t* status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
+  RouteArgs r;
+  r.M = M; r.H = H; r.E = E; r.k = k; r.renorm = a.renormalize ? 1 : 0;
+  r.has_shared = a.shared_blob ? 1 : 0;
+  r.numel = numel; r.cap = s.cap; r.max_blocks = s.max_blocks; r.max_seg = s.max_seg;
+  r.max_ws = w.max_ws;
+  r.logits = a.router_logits;
+  r.x = a.hidden_states;
+  r.gate_w = a.shared_gate_weight;
   if (a.router_logits) {
-    float* w_out = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
-    int32_t* i_out = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
-    int r = launch_router_topk(a.router_logits, M, E, k, a.renormalize ? 1 : 0, w_out, i_out,
-                               nullptr, st);
-    if (r != MTP_OK) return r;
-    tw = w_out;
-    tid = i_out;
+    r.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
+    r.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
+  } else {
+    r.topk_w = const_cast<float*>(a.topk_weights);
+    r.topk_ids = const_cast<int32_t*>(a.topk_ids);
   }
-  int r = launch_moe_align(tid, numel, E, kLayerBM, nullptr, 0, s.cap, s.max_blocks, s.max_seg,
-                           sorted, eids, ntpp, segs, nseg, st);
-  if (r != MTP_OK) return r;
+  r.gate = reinterpret_cast<float*>(ws + w.gate);
+  r.sorted = sorted; r.eids = eids; r.ntpp = ntpp; r.segs = segs; r.nseg = nseg;
+  r.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
+  r.nws = reinterpret_cast<int32_t*>(ws + w.nws);
+  r.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);
+  r.done = reinterpret_cast<int32_t*>(ws + w.done);
+  r.blobs = a.expert_blobs; r.expert_bytes = a.expert_bytes;
+  r.slot_table = a.slot_table; r.host_blobs = a.host_blobs; r.shared_blob = a.shared_blob;
+  r.status = status;
+  r.demand_log = a.demand_log;
 
-  MoeDevArgs d;
-  d.M = M; d.H = H; d.I = I; d.E = E; d.k = k; d.zero_mode = a.zero_mode;
-  d.numel = numel; d.max_seg = s.max_seg; d.has_shared = a.shared_blob ? 1 : 0;
-  d.x = a.hidden_states; d.topk_w = tw; d.topk_ids = tid;
-  d.sorted = sorted; d.segs = segs; d.nseg = nseg;
-  d.blobs = a.expert_blobs; d.expert_bytes = a.expert_bytes;
-  d.slot_table = a.slot_table; d.host_blobs = a.host_blobs; d.shared_blob = a.shared_blob;
-  d.L = L;
-  d.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
-  d.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
-  d.status = a.status;
-  return launch_moe_decode(d, G, a.shared_gate_weight, a.out, a.out_f32, a.demand_log, st);
+  FusedArgs f;
+  f.M = M; f.H = H; f.I = I; f.E = E; f.k = k; f.numel = numel; f.zero_mode = a.zero_mode;
+  f.has_shared = r.has_shared; f.G = G;
+  f.x = a.hidden_states; f.topk_w = r.topk_w; f.topk_ids = r.topk_ids;
+  f.wseg = r.wseg; f.nws = r.nws;
+  f.L = L;
+  f.gate = r.gate; f.seg_done = r.seg_done; f.done = r.done;
+  f.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
+  f.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
+  f.out = a.out; f.out_f32 = a.out_f32;
+  f.status = status;
+  f.stages = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
+  return launch_moe_fused(f, r, st);
 }
 
 }  // extern "C"

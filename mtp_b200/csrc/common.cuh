@@ -258,6 +258,52 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   return v;
 }
 
+// int8 MMA m16n8k32, exact int32 accumulation: A = unsigned 4-bit weights held
+// as u8, B = the high (signed) or low (unsigned) byte of 16-bit activations.
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_u8s8_zc(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_u8u8_zc(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Two packed weight words (row g and row g+8 of one k32 step, kernel layout in
+// gptq.cu) -> the four u8 A registers of an m16n8k32 tile: the low nibbles of
+// each byte are k = 4t..4t+3, the high nibbles k = 16+4t..16+4t+3. One
+// volatile block so it is not hoisted across the unrolled loop.
+__device__ __forceinline__ void unpack_u8(uint32_t wg, uint32_t wg8, uint32_t (&a)[4]) {
+  asm volatile(
+      "{\n"
+      ".reg .b32 t0, t1;\n"
+      "and.b32 %0, %4, 0x0F0F0F0F;\n"
+      "and.b32 %1, %5, 0x0F0F0F0F;\n"
+      "shr.u32 t0, %4, 4;\n"
+      "shr.u32 t1, %5, 4;\n"
+      "and.b32 %2, t0, 0x0F0F0F0F;\n"
+      "and.b32 %3, t1, 0x0F0F0F0F;\n"
+      "}\n"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+      : "r"(wg), "r"(wg8));
+}
+
 // MMA with a zero C operand (starts a fresh per-chunk partial).
 __device__ __forceinline__ void mma_bf16_16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                                   uint32_t b1) {

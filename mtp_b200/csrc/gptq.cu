@@ -9,12 +9,13 @@
 // Kernel layout (this build's own; one expert = one contiguous blob so that a
 // slot fill is a single copy):
 //   weights  [N/16 strips][K/64 chunks][32 lanes][4 words]: the 16 bytes lane l
-//            reads for (strip s, chunk c) are exactly its A fragments of the
-//            four m16n8k16 tiles covering rows 16s..16s+15, k 64c..64c+63.
-//            Word kk of lane l (g = l/4, t = l%4, kb = 64c + 16kk + 2t,
-//            r0 = 16s + g, r1 = r0 + 8) holds, nibble 0..7:
-//            (r0,kb) (r1,kb) (r0,kb+8) (r1,kb+8) (r0,kb+1) (r1,kb+1) (r0,kb+9) (r1,kb+9)
-//            so nibbles j and j+4 form A register j (see common.cuh).
+//            reads for (strip s, chunk c) hold its A operands of the two
+//            m16n8k32 (8-bit) tiles covering rows 16s..16s+15, k 64c..64c+63.
+//            Word kk of lane l (g = l/4, t = l%4, row r = 16s + g + 8(kk&1),
+//            kb = 64c + 32(kk>>1)) holds, in byte b = 0..3, the nibble pair
+//            low = q(r, kb + 4t + b), high = q(r, kb + 16 + 4t + b),
+//            so `w & 0x0F0F0F0F` and `(w >> 4) & 0x0F0F0F0F` are the u8 A
+//            registers for k = kb+4t..+3 and kb+16+4t..+3 (see common.cuh).
 //   scales   [N/16][K/G][8][2] fp16: for (strip, group), lane group g reads one
 //            32-bit word = (scale of row g, scale of row g+8).
 //   zeros    [N/16][K/G][8] bytes: byte g = zero(row g) | zero(row g+8) << 4.
@@ -67,16 +68,13 @@ __global__ void repack_qweight_kernel(const int32_t* __restrict__ gq, int N, int
   const int c = static_cast<int>(rest % chunks);
   const int s = static_cast<int>(rest / chunks);
   const int g = l >> 2, t = l & 3;
-  const int kb = 64 * c + 16 * kk + 2 * t;
-  const int r0 = 16 * s + g, r1 = r0 + 8;
+  const int r = 16 * s + g + 8 * (kk & 1);
+  const int kb = 64 * c + 32 * (kk >> 1) + 4 * t;
   const int32_t* q = gq + static_cast<int64_t>(e) * (K / 8) * N;
-  const uint32_t word = gptq_nib_rows(q, N, kb, r0) | gptq_nib_rows(q, N, kb, r1) << 4 |
-                        gptq_nib_rows(q, N, kb + 8, r0) << 8 |
-                        gptq_nib_rows(q, N, kb + 8, r1) << 12 |
-                        gptq_nib_rows(q, N, kb + 1, r0) << 16 |
-                        gptq_nib_rows(q, N, kb + 1, r1) << 20 |
-                        gptq_nib_rows(q, N, kb + 9, r0) << 24 |
-                        gptq_nib_rows(q, N, kb + 9, r1) << 28;
+  uint32_t word = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    word |= (gptq_nib_rows(q, N, kb + b, r) | gptq_nib_rows(q, N, kb + 16 + b, r) << 4) << (8 * b);
   reinterpret_cast<uint32_t*>(blobs + e * stride + off)[w] = word;
 }
 

@@ -5,26 +5,6 @@
 
 namespace mtp {
 
-// Device-side arguments of one W4A16 MoE layer call (decode kernels).
-struct MoeDevArgs {
-  int M, H, I, E, k, zero_mode, numel, max_seg, has_shared;
-  const uint16_t* x;          // [M, H] bf16
-  const float* topk_w;        // [M*k]
-  const int32_t* topk_ids;    // [M*k]
-  const int32_t* sorted;      // sorted_token_ids (block size 8)
-  const int32_t* segs;        // [max_seg][3] (expert, first block, block count)
-  const int32_t* nseg;        // [1]
-  const uint8_t* blobs;       // resident expert blobs (slot-indexed)
-  int64_t expert_bytes;
-  const int32_t* slot_table;  // [E] or NULL
-  const uint8_t* host_blobs;  // device-mapped pinned host store or NULL
-  const uint8_t* shared_blob; // or NULL
-  MtpExpertLayout L;
-  uint16_t* hbuf;             // [numel + M, I] bf16
-  float* ybuf;                // [numel + M, H] fp32
-  int32_t* status;            // [4] or NULL
-};
-
 // Work segment: kWsBlocks token block(s) of one expert (or of the shared
 // expert), written by the route kernel and copied into shared memory by the
 // fused kernel. 12 ints = 48 bytes (16-byte multiple). One block per segment
@@ -95,8 +75,6 @@ int repack_gptq(const int32_t* w13q, const int32_t* w13z, const uint16_t* w13s, 
                 cudaStream_t st);
 int gptq_dequant(const int32_t* q, const int32_t* z, const uint16_t* s, const int32_t* gidx, int K,
                  int N, int G, int zero_mode, float* out, cudaStream_t st);
-int launch_moe_decode(const MoeDevArgs& a, int G, const uint16_t* gate_w, uint16_t* out,
-                      float* out_f32, int32_t* demand_log, cudaStream_t st);
 
 bool fused_supported(int H, int I, int G);
 int fused_max_work_segments(int M, int max_seg, int max_blocks);

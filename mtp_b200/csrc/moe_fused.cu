@@ -65,6 +65,7 @@ constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
 constexpr int kRedBytes = kCW * 2 * 4 * 32 * 4 + 2 * 4 * 32 * 4;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per layer call
 constexpr int kBarConsumers = 1;   // named barrier id for the consumer warps
+constexpr int kMaxChunks = 32;     // K / 64 for K <= 2048
 
 // ---------------------------------------------------------------------------
 // shared-memory control block and the per-pass work-segment view
@@ -289,39 +290,118 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
 // ---------------------------------------------------------------------------
 // consumers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void zero_bias_from_byte(uint32_t zb, int zero_mode, uint32_t& lo, uint32_t& hi) {
-  if (zero_mode == MTP_ZERO_SYM8) {
-    lo = hi = zero_bias_pair(8);
-  } else {
-    lo = zero_bias_pair(zb & 0xF);
-    hi = zero_bias_pair(zb >> 4);
-  }
-}
+// Per operand buffer: quantisation metadata of its 8 rows.
+struct OperandMeta {
+  float sx[kFBM];              // row scale: x = sx * (256 * hi + lo)
+  float amax[kFBM][2];         // per-half row maxima (scratch)
+  int xsum[kFBM][kMaxChunks];  // per 64-wide chunk: sum of the 16-bit row values
+};
 
 __device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-__device__ __forceinline__ void fold(float (&acc)[4], const float (&d)[4], uint32_t scw) {
+// Quantise the 8 bf16 rows of an operand buffer in place into 16-bit
+// integers split into a signed high byte row and an unsigned low byte row
+// (row n: hi at [0, K), lo at [K, 2K) of its 2K + 16 byte slot), with a
+// per-row scale and per-64-element-chunk sums. 512 consumer threads, 64 per
+// row; thread tr owns the 4-element groups j = tr + 64 i, so every shared-
+// memory access of a warp is contiguous. All values are read before the first
+// barrier and written after it (the output overlaps the input).
+__device__ __forceinline__ void quantize_rows(uint8_t* rows, OperandMeta& meta, int K, int ctid) {
+  const int n = ctid >> 6, tr = ctid & 63;
+  const int ng = K / 4;  // 16..512 groups per row
+  uint8_t* row = rows + n * (2u * K + 16u);
+  uint2 raw[8];  // bf16 pairs, kept packed until the scale is known
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = tr + 64 * i;
+    raw[i] = make_uint2(0u, 0u);
+    if (j < ng) {
+      raw[i] = *reinterpret_cast<const uint2*>(row + 8 * j);
+      const uint32_t m0 = __vmaxu2(raw[i].x & 0x7fff7fffu, raw[i].y & 0x7fff7fffu);
+      mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
+    }
+  }
+  mx = warp_max(mx);
+  if ((ctid & 31) == 0) meta.amax[n][(ctid >> 5) & 1] = mx;
+  named_bar_sync(kBarConsumers, kCT);
+  const float amax = fmaxf(meta.amax[n][0], meta.amax[n][1]);
+  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (64 * i < ng) {  // warp-uniform: ng is a multiple of 16, the shuffles stay converged
+      const int j = tr + 64 * i;
+      int sum = 0;
+      if (j < ng) {
+        uint32_t hw = 0u, lw = 0u;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t h = (b < 2 ? raw[i].x : raw[i].y) >> (16 * (b & 1));
+          const int q = max(-32767, min(32767, __float2int_rn(__uint_as_float(h << 16) * inv)));
+          sum += q;
+          hw |= (static_cast<uint32_t>(q >> 8) & 0xffu) << (8 * b);
+          lw |= (static_cast<uint32_t>(q) & 0xffu) << (8 * b);
+        }
+        *reinterpret_cast<uint32_t*>(row + 4 * j) = hw;
+        *reinterpret_cast<uint32_t*>(row + K + 4 * j) = lw;
+      }
+      // a 64-element chunk is the 16 groups of 16 consecutive lanes
+      sum += __shfl_xor_sync(kFullMask, sum, 1);
+      sum += __shfl_xor_sync(kFullMask, sum, 2);
+      sum += __shfl_xor_sync(kFullMask, sum, 4);
+      sum += __shfl_xor_sync(kFullMask, sum, 8);
+      if ((tr & 15) == 0 && j < ng) meta.xsum[n][j >> 4] = sum;
+    }
+  }
+  if (tr == 0) meta.sx[n] = amax / 32767.f;
+  named_bar_sync(kBarConsumers, kCT);
+}
+
+// B operands (high and low byte rows) of one k32 step for this lane's
+// ldmatrix row: matrices hi[k0..], hi[k0+16..], lo[k0..], lo[k0+16..].
+__device__ __forceinline__ void load_b(uint32_t xbase, uint32_t rs, int K, int row, int mat, int k0,
+                                       uint32_t (&b)[4]) {
+  const uint32_t addr = xbase + row * rs + (mat >= 2 ? K : 0) + k0 + 16 * (mat & 1);
+  ldsm_x4(addr, b[0], b[1], b[2], b[3]);
+}
+
+__device__ __forceinline__ void zero_rows_of(uint32_t zb, int zero_mode, int& z0, int& z1) {
+  if (zero_mode == MTP_ZERO_SYM8) {
+    z0 = z1 = 8;
+  } else {
+    z0 = zb & 0xF;
+    z1 = zb >> 4;
+  }
+}
+
+// acc += s_row * (256 * hi + lo - z_row * xsum_col) for the 4 accumulator
+// elements of this lane (rows g, g+8; columns 2t, 2t+1).
+__device__ __forceinline__ void fold_int(float (&acc)[4], const int (&dh)[4], const int (&dl)[4], uint32_t scw,
+                                         int z0, int z1, int xs0, int xs1) {
   const float2 s = half2_bits_to_float2(scw);
-  acc[0] = fmaf(s.x, d[0], acc[0]);
-  acc[1] = fmaf(s.x, d[1], acc[1]);
-  acc[2] = fmaf(s.y, d[2], acc[2]);
-  acc[3] = fmaf(s.y, d[3], acc[3]);
+  acc[0] = fmaf(static_cast<float>(256 * dh[0] + dl[0] - z0 * xs0), s.x, acc[0]);
+  acc[1] = fmaf(static_cast<float>(256 * dh[1] + dl[1] - z0 * xs1), s.x, acc[1]);
+  acc[2] = fmaf(static_cast<float>(256 * dh[2] + dl[2] - z1 * xs0), s.y, acc[2]);
+  acc[3] = fmaf(static_cast<float>(256 * dh[3] + dl[3] - z1 * xs1), s.y, acc[3]);
 }
 
 template <int W1C, int W2C>
 __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages, uint8_t* xbufs,
-                          float* red, uint64_t deadline) {
+                          OperandMeta* metas, float* red, uint64_t deadline) {
   const int ctid = threadIdx.x;  // 0..511
   const int warp = ctid >> 5, lane = ctid & 31, g = lane >> 2, t = lane & 3;
   const int nkw = a.H / 64 / W1C;  // warps along K in W1 (<= 16)
+  const int cpg = a.G / 64;        // 64-wide chunks per quantisation group
   int st = 0, xb = 0;
   uint32_t ph = 0, xph = 0;
   const int ld_row = lane & 7, ld_mat = lane >> 3;  // ldmatrix row address of this lane
 
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
+    const int K = pass == 0 ? a.H : a.I;
+    const uint32_t rs = 2u * K + 16u;
     for (int u = P.ub; u < P.ue; ++u) {
       const int seg = u / P.per, idx = u % P.per;
       const int* e = ws_entry(P, seg);
@@ -332,54 +412,60 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
       const bool wvalid = cb.stage_valid[st] != 0;
       const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
       for (int blk = 0; blk < nb; ++blk) {
-        if (!reuse && !mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && ctid == 0) record_timeout(a);
-        const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
+        OperandMeta& meta = metas[xb];
+        uint8_t* xrows = xbufs + xb * a.xbuf_bytes;
+        if (!reuse) {
+          if (!mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && ctid == 0) record_timeout(a);
+          quantize_rows(xrows, meta, K, ctid);
+        }
+        const uint32_t xbase = smem_u32(xrows);
         const int* cols = e + 4 + blk * kFBM;
         if (pass == 0) {
           // ------------------------------ W1 ------------------------------
-          const uint32_t rs = 2u * a.H + 16u;
           float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
           if (wvalid && warp < nkw) {
             const uint32_t sb = 8u * a.H, scb = (a.H / a.G) * 32u, zpb = (a.H / a.G) * 8u;
-            // all operands of the warp's W1C chunks x 2 strips first, then the
-            // MMAs interleaved over 2*W1C independent accumulators
-            uint4 w[W1C][2];
-            uint32_t bf[W1C][8];
-            uint32_t zlo[W1C][2], zhi[W1C][2], scw[W1C][2];
+            int dh[2][4], dl[2][4];
+            int xs0 = 0, xs1 = 0;
 #pragma unroll
             for (int j = 0; j < W1C; ++j) {
               const int c = warp * W1C + j;
-              const int grp = c * 64 / a.G;
-              const uint32_t xa = xbase + ld_row * rs + (64 * c + 8 * ld_mat) * 2;
-              ldsm_x4(xa, bf[j][0], bf[j][1], bf[j][2], bf[j][3]);
-              ldsm_x4(xa + 64, bf[j][4], bf[j][5], bf[j][6], bf[j][7]);
+              uint4 w[2];
+              w[0] = lds128(sbase + (c * 32 + lane) * 16);
+              w[1] = lds128(sbase + sb + (c * 32 + lane) * 16);
 #pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                w[j][q] = lds128(sbase + q * sb + (c * 32 + lane) * 16);
-                scw[j][q] = lds32(sbase + 2 * sb + q * scb + (grp * 8 + g) * 4);
-                const uint32_t zb =
-                    a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 2 * sb + 2 * scb + q * zpb + grp * 8 + g) : 0x88u;
-                zero_bias_from_byte(zb, a.zero_mode, zlo[j][q], zhi[j][q]);
-              }
-            }
-            float d[W1C][2][4];
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-              for (int j = 0; j < W1C; ++j)
+              for (int s2 = 0; s2 < 2; ++s2) {
+                uint32_t b[4];
+                load_b(xbase, rs, K, ld_row, ld_mat, 64 * c + 32 * s2, b);
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                   uint32_t A[4];
-                  dequant_word(pick(w[j][q], kk), zlo[j][q], zhi[j][q], A);
-                  if (kk == 0)
-                    mma_bf16_16816_zc(d[j][q], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
-                  else
-                    mma_bf16_16816(d[j][q], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+                  unpack_u8(pick(w[q], 2 * s2), pick(w[q], 2 * s2 + 1), A);
+                  if (s2 == 0 && (j == 0 || c % cpg == 0)) {
+                    imma_u8s8_zc(dh[q], A, b[0], b[1]);
+                    imma_u8u8_zc(dl[q], A, b[2], b[3]);
+                  } else {
+                    imma_u8s8(dh[q], A, b[0], b[1]);
+                    imma_u8u8(dl[q], A, b[2], b[3]);
+                  }
                 }
+              }
+              xs0 += meta.xsum[2 * t][c];
+              xs1 += meta.xsum[2 * t + 1][c];
+              if ((c + 1) % cpg == 0 || j == W1C - 1) {
+                const int grp = c / cpg;
 #pragma unroll
-            for (int j = 0; j < W1C; ++j)
-#pragma unroll
-              for (int q = 0; q < 2; ++q) fold(acc[q], d[j][q], scw[j][q]);
+                for (int q = 0; q < 2; ++q) {
+                  const uint32_t scw = lds32(sbase + 2 * sb + q * scb + (grp * 8 + g) * 4);
+                  const uint32_t zb =
+                      a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 2 * sb + 2 * scb + q * zpb + grp * 8 + g) : 0x88u;
+                  int z0, z1;
+                  zero_rows_of(zb, a.zero_mode, z0, z1);
+                  fold_int(acc[q], dh[q], dl[q], scw, z0, z1, xs0, xs1);
+                }
+                xs0 = xs1 = 0;
+              }
+            }
           }
           if (!keep) {
             __syncwarp();
@@ -402,57 +488,71 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
             const float up = __shfl_xor_sync(kFullMask, v, 2);
             if (sub == 0) {
               const int r = m >> 5, l = m & 31;
-              const int p = cols[2 * (l & 3) + (r & 1)];
+              const int col = 2 * (l & 3) + (r & 1);
+              const int p = cols[col];
               if (p >= 0) {
                 const int row = (l >> 2) + 8 * (r >> 1);
+                const float sx = meta.sx[col];
                 a.hbuf[static_cast<int64_t>(p) * a.I + 16 * idx + row] =
-                    __bfloat16_as_ushort(__float2bfloat16(silu(v) * up));
+                    __bfloat16_as_ushort(__float2bfloat16(silu(v * sx) * (up * sx)));
               }
             }
           }
-          // the barrier protects red from the next unit and orders the h stores
-          // before the release below
+          // protects red from the next unit and orders the h stores before the
+          // release below
           named_bar_sync(kBarConsumers, kCT);
           if (blk == nb - 1 && ctid == 0) red_release_gpu_add(a.seg_done + seg, 1);
         } else {
           // ------------------------------ W2 ------------------------------
-          const uint32_t rs = 2u * a.I + 16u;
           const int sidx = warp >> 1, hk = warp & 1;
           float acc[4] = {0.f, 0.f, 0.f, 0.f};
           if (wvalid) {
             const uint32_t sb = 8u * a.I;  // one strip over K = I
             const uint32_t scb_all = 8u * (a.I / a.G) * 32u;
             const int gper = a.I / a.G;
-            uint4 w[W2C];
-            uint32_t bf[W2C][8];
-            uint32_t zlo[W2C], zhi[W2C], scw[W2C];
+            int dh[2][4], dl[2][4];  // two independent chains: chunk parity
+            int xs0 = 0, xs1 = 0;
+            bool fresh[2] = {true, true};
 #pragma unroll
             for (int j = 0; j < W2C; ++j) {
               const int c = hk * W2C + j;
-              const int grp = c * 64 / a.G;
-              const uint32_t xa = xbase + ld_row * rs + (64 * c + 8 * ld_mat) * 2;
-              ldsm_x4(xa, bf[j][0], bf[j][1], bf[j][2], bf[j][3]);
-              ldsm_x4(xa + 64, bf[j][4], bf[j][5], bf[j][6], bf[j][7]);
-              w[j] = lds128(sbase + sidx * sb + (c * 32 + lane) * 16);
-              scw[j] = lds32(sbase + 8 * sb + ((sidx * gper + grp) * 8 + g) * 4);
-              const uint32_t zb =
-                  a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 8 * sb + scb_all + (sidx * gper + grp) * 8 + g) : 0x88u;
-              zero_bias_from_byte(zb, a.zero_mode, zlo[j], zhi[j]);
-            }
-            float d[W2C][4];
+              const int par = j & 1;
+              const uint4 w = lds128(sbase + sidx * sb + (c * 32 + lane) * 16);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-              for (int j = 0; j < W2C; ++j) {
+              for (int s2 = 0; s2 < 2; ++s2) {
+                uint32_t b[4];
+                load_b(xbase, rs, K, ld_row, ld_mat, 64 * c + 32 * s2, b);
                 uint32_t A[4];
-                dequant_word(pick(w[j], kk), zlo[j], zhi[j], A);
-                if (kk == 0)
-                  mma_bf16_16816_zc(d[j], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
-                else
-                  mma_bf16_16816(d[j], A, bf[j][2 * kk], bf[j][2 * kk + 1]);
+                unpack_u8(pick(w, 2 * s2), pick(w, 2 * s2 + 1), A);
+                if (s2 == 0 && fresh[par]) {
+                  imma_u8s8_zc(dh[par], A, b[0], b[1]);
+                  imma_u8u8_zc(dl[par], A, b[2], b[3]);
+                } else {
+                  imma_u8s8(dh[par], A, b[0], b[1]);
+                  imma_u8u8(dl[par], A, b[2], b[3]);
+                }
               }
+              fresh[par] = false;
+              xs0 += meta.xsum[2 * t][c];
+              xs1 += meta.xsum[2 * t + 1][c];
+              if ((c + 1) % cpg == 0 || j == W2C - 1) {
+                const int grp = c / cpg;
+                const uint32_t scw = lds32(sbase + 8 * sb + ((sidx * gper + grp) * 8 + g) * 4);
+                const uint32_t zb =
+                    a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 8 * sb + scb_all + (sidx * gper + grp) * 8 + g) : 0x88u;
+                int z0, z1;
+                zero_rows_of(zb, a.zero_mode, z0, z1);
+                int sh[4], sl[4];
 #pragma unroll
-            for (int j = 0; j < W2C; ++j) fold(acc, d[j], scw[j]);
+                for (int r = 0; r < 4; ++r) {
+                  sh[r] = (fresh[0] ? 0 : dh[0][r]) + (fresh[1] ? 0 : dh[1][r]);
+                  sl[r] = (fresh[0] ? 0 : dl[0][r]) + (fresh[1] ? 0 : dl[1][r]);
+                }
+                fold_int(acc, sh, sl, scw, z0, z1, xs0, xs1);
+                xs0 = xs1 = 0;
+                fresh[0] = fresh[1] = true;
+              }
+            }
           }
           if (!keep) {
             __syncwarp();
@@ -465,8 +565,8 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
           named_bar_sync(kBarConsumers, kCT);
           if (hk == 0) {
             const int p0 = cols[2 * t], p1 = cols[2 * t + 1];
-            const float w0 = (p0 >= 0 && p0 < a.numel) ? a.topk_w[p0] : 1.f;
-            const float w1 = (p1 >= 0 && p1 < a.numel) ? a.topk_w[p1] : 1.f;
+            const float w0 = ((p0 >= 0 && p0 < a.numel) ? a.topk_w[p0] : 1.f) * meta.sx[2 * t];
+            const float w1 = ((p1 >= 0 && p1 < a.numel) ? a.topk_w[p1] : 1.f) * meta.sx[2 * t + 1];
             const int nbase = 128 * idx + 16 * sidx;
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -553,7 +653,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a
   int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
   uint8_t* stages = smem + kCtrlBytes + kTableBytes;
   uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
-  float* red = reinterpret_cast<float*>(xbufs + 2 * a.xbuf_bytes);
+  OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
+  float* red = reinterpret_cast<float*>(metas + 2);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.stages; ++i) {
@@ -596,7 +697,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a
   } else if (warp == kBProd) {
     operand_producer(a, cb, table, xbufs, deadline);
   } else {
-    consumers<W1C, W2C>(a, cb, table, stages, xbufs, red, deadline);
+    consumers<W1C, W2C>(a, cb, table, stages, xbufs, metas, red, deadline);
   }
 }
 
@@ -762,7 +863,7 @@ static FusedGeometry fused_geometry(int H, int I, int G) {
   f.stage_bytes = round128(w1 > w2 ? w1 : w2);
   const int maxrow = H > I ? H : I;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (2ull * maxrow + 16));
-  const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + kRedBytes;
+  const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2ull * sizeof(OperandMeta) + kRedBytes;
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;
@@ -809,12 +910,12 @@ static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream
   return MTP_OK;
 }
 
+// W1C: 64-wide K chunks per W1 warp (H/64 chunks over at most 16 warps);
+// W2C: chunks per W2 warp (two warps per strip split K = I).
 static bool fused_template(int H, int I, int* w1c, int* w2c) {
-  *w1c = H <= 1024 ? 1 : H / 1024;
+  *w1c = H > 1024 ? 2 : 1;
   *w2c = I / 128;
-  const bool w1ok = *w1c == 1 || *w1c == 2 || *w1c == 4;
-  const bool w2ok = *w2c == 1 || *w2c == 2 || *w2c == 4 || *w2c == 6 || *w2c == 8;
-  return w1ok && w2ok && H / 64 / *w1c <= kCW;
+  return (H / 64) % *w1c == 0 && H / 64 / *w1c <= kCW && *w2c >= 1 && *w2c <= 8;
 }
 
 bool fused_supported(int H, int I, int G) {
@@ -869,14 +970,20 @@ int launch_moe_fused(const FusedArgs& a_in, const RouteArgs& r, cudaStream_t st)
   if (w1c == A && w2c == B) return launch_fused_t<A, B>(a, f, st);
   MTP_FUSED_CASE(1, 1)
   MTP_FUSED_CASE(1, 2)
+  MTP_FUSED_CASE(1, 3)
   MTP_FUSED_CASE(1, 4)
+  MTP_FUSED_CASE(1, 5)
+  MTP_FUSED_CASE(1, 6)
+  MTP_FUSED_CASE(1, 7)
+  MTP_FUSED_CASE(1, 8)
   MTP_FUSED_CASE(2, 1)
   MTP_FUSED_CASE(2, 2)
+  MTP_FUSED_CASE(2, 3)
   MTP_FUSED_CASE(2, 4)
+  MTP_FUSED_CASE(2, 5)
   MTP_FUSED_CASE(2, 6)
+  MTP_FUSED_CASE(2, 7)
   MTP_FUSED_CASE(2, 8)
-  MTP_FUSED_CASE(4, 4)
-  MTP_FUSED_CASE(4, 8)
 #undef MTP_FUSED_CASE
   return MTP_ERR_SHAPE;
 }

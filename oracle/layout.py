@@ -38,21 +38,20 @@ def repack_projection(qweight: np.ndarray, qzeros: np.ndarray, scales: np.ndarra
     s = np.ascontiguousarray(scales).view(np.uint16)  # [K/G, N]
     k, n = q.shape
     strips, chunks, groups = n // 16, k // 64, k // group
-    # words[s, c, lane, kk]
+    # words[s, c, lane, kk]: row 16s + g + 8(kk & 1), k base 64c + 32(kk >> 1) + 4t;
+    # byte b = q(row, kb + b) | q(row, kb + 16 + b) << 4
     lane = np.arange(32)
     g, t = lane // 4, lane % 4
     words = np.zeros((strips, chunks, 32, 4), dtype=np.uint32)
     for si in range(strips):
-        r0 = 16 * si + g
-        r1 = r0 + 8
         for c in range(chunks):
             for kk in range(4):
-                kb = 64 * c + 16 * kk + 2 * t
-                nibs = [q[kb, r0], q[kb, r1], q[kb + 8, r0], q[kb + 8, r1],
-                        q[kb + 1, r0], q[kb + 1, r1], q[kb + 9, r0], q[kb + 9, r1]]
+                r = 16 * si + g + 8 * (kk & 1)
+                kb = 64 * c + 32 * (kk >> 1) + 4 * t
                 w = np.zeros(32, dtype=np.uint32)
-                for i, v in enumerate(nibs):
-                    w |= v.astype(np.uint32) << np.uint32(4 * i)
+                for b in range(4):
+                    byte = q[kb + b, r].astype(np.uint32) | (q[kb + 16 + b, r].astype(np.uint32) << np.uint32(4))
+                    w |= byte << np.uint32(8 * b)
                 words[si, c, :, kk] = w
     sc = np.zeros((strips, groups, 8, 2), dtype=np.uint16)
     zp = np.zeros((strips, groups, 8), dtype=np.uint8)
@@ -92,21 +91,19 @@ def decode_projection(blob: np.ndarray, off_q: int, off_s: int, off_z: int, n: i
     lane = np.arange(32)
     g, t = lane // 4, lane % 4
     for si in range(strips):
-        r0 = 16 * si + g
-        r1 = r0 + 8
         for c in range(chunks):
             for kk in range(4):
                 w = words[si, c, :, kk]
-                kb = 64 * c + 16 * kk + 2 * t
-                coords = [(r0, kb), (r1, kb), (r0, kb + 8), (r1, kb + 8),
-                          (r0, kb + 1), (r1, kb + 1), (r0, kb + 9), (r1, kb + 9)]
-                for i, (rr, kc) in enumerate(coords):
-                    qv = ((w >> np.uint32(4 * i)) & np.uint32(0xF)).astype(np.float32)
-                    grp = kc // group
-                    zbyte = zp[si, grp, g]
-                    zrow = np.where(rr == r0, zbyte & 0xF, zbyte >> 4).astype(np.float32)
-                    if zero_mode == "sym8":
-                        zrow = np.float32(8.0)
-                    srow = np.where(rr == r0, sc[si, grp, g, 0], sc[si, grp, g, 1]).astype(np.float32)
-                    out[rr, kc] = (qv - zrow) * srow
+                rr = 16 * si + g + 8 * (kk & 1)
+                kb = 64 * c + 32 * (kk >> 1) + 4 * t
+                for b in range(4):
+                    byte = (w >> np.uint32(8 * b)) & np.uint32(0xFF)
+                    for kc, qv in ((kb + b, byte & np.uint32(0xF)), (kb + 16 + b, byte >> np.uint32(4))):
+                        grp = kc // group
+                        zbyte = zp[si, grp, g]
+                        zrow = np.where((kk & 1) == 0, zbyte & 0xF, zbyte >> 4).astype(np.float32)
+                        if zero_mode == "sym8":
+                            zrow = np.float32(8.0)
+                        srow = np.where((kk & 1) == 0, sc[si, grp, g, 0], sc[si, grp, g, 1]).astype(np.float32)
+                        out[rr, kc] = (qv.astype(np.float32) - zrow) * srow
     return out
