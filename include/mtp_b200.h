@@ -174,7 +174,13 @@ typedef struct MtpMoeLayerArgs {
                                       host_blobs, [1] misses with no host store
                                       (expert output zeroed), [2],[3] reserved;
                                       accumulated, the caller zeroes it        */
-  void* workspace;
+  void* workspace;                 /* device, 256-byte aligned, at least
+                                      mtp_w4a16_moe_layer_workspace_size()
+                                      bytes, ZERO-FILLED before its first use:
+                                      the layer keeps its per-call counters
+                                      there and every call leaves them zero
+                                      again (re-zero it after a call that
+                                      reported a timeout in status[2])       */
   int64_t workspace_bytes;
 } MtpMoeLayerArgs;
 
@@ -196,7 +202,7 @@ MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
  * address (with that device current), so make it before any stream capture.
  * All calls share the array and it keeps the last call's contents; calls that
  * overlap on the GPU race and must be serialised by the caller.            */
-#define MTP_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define MTP_NOALLOC_SCRATCH_BYTES (5u << 20)
 MTP_API int mtp_w4a16_moe_layer_noalloc(const MtpMoeLayerArgs* args, void* stream);
 
 #ifdef __cplusplus

@@ -23,10 +23,15 @@ static AlignSizes align_sizes(int numel, int E, int BM, int pad) {
   return s;
 }
 
-// Workspace of the layer call, each region 256-byte aligned.
+// Workspace of the layer call, each region 256-byte aligned. The first
+// regions (grid barrier, per-expert counts, per-segment counters) have fixed
+// offsets and sizes, the same for every call shape, so one workspace can serve
+// calls of any size: they must be zero before the first call, and every call
+// that completes leaves them zero again.
+constexpr int kMaxExpertsWs = 1024;
+constexpr int kMaxWorkSegments = 32768;
 struct LayerWs {
-  int64_t tw, tid, sorted, eids, ntpp, segs, nseg, gate, wseg, nws, seg_done, done, status, hbuf, ybuf,
-      total;
+  int64_t bar, cnt, seg_done, tw, tid, lists, gate, wseg, status, hbuf, ybuf, total;
   int max_ws;
 };
 
@@ -41,18 +46,14 @@ static LayerWs layer_ws(int M, int E, int k, int H, int I) {
     o = round_up(o + bytes, 256);
     return at;
   };
+  w.bar = take(8);
+  w.cnt = take(4LL * kMaxExpertsWs);
+  w.seg_done = take(4LL * kMaxWorkSegments);
   w.tw = take(4LL * numel);
   w.tid = take(4LL * numel);
-  w.sorted = take(4LL * s.cap);
-  w.eids = take(4LL * s.max_blocks);
-  w.ntpp = take(4);
-  w.segs = take(12LL * s.max_seg);
-  w.nseg = take(4);
+  w.lists = take(4LL * E * M);
   w.gate = take(4LL * M);
   w.wseg = take(4LL * kWsInts * w.max_ws);
-  w.nws = take(4);
-  w.seg_done = take(4LL * w.max_ws);
-  w.done = take(4);
   w.status = take(16);
   w.hbuf = take(2LL * (numel + M) * I);
   w.ybuf = take(4LL * (numel + M) * H);
@@ -205,60 +206,43 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
       (a.shared_blob && !aligned(a.shared_blob, 256)) || (a.out_f32 && !aligned(a.out_f32, 16)))
     return MTP_ERR_ALIGN;
   const LayerWs w = layer_ws(M, E, k, H, I);
+  if (w.max_ws > kMaxWorkSegments) return MTP_ERR_SHAPE;
   if (a.workspace_bytes < w.total) return MTP_ERR_WORKSPACE;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned char* ws = static_cast<unsigned char*>(a.workspace);
   const int numel = M * k;
-  const AlignSizes s = align_sizes(numel, E, kLayerBM, 0);
-
-  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
-  int32_t* eids = reinterpret_cast<int32_t*>(ws + w.eids);
-  int32_t* ntpp = reinterpret_cast<int32_t*>(ws + w.ntpp);
-  int32_t* segs = reinterpret_cast<int32_t*>(ws + w.segs);
-  int32_t* nseg = reinterpret_cast<int32_t*>(ws + w.nseg);
-
   if (!fused_supported(H, I, G)) return MTP_ERR_SHAPE;
-  int32_t* status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
-  RouteArgs r;
-  r.M = M; r.H = H; r.E = E; r.k = k; r.renorm = a.renormalize ? 1 : 0;
-  r.has_shared = a.shared_blob ? 1 : 0;
-  r.numel = numel; r.cap = s.cap; r.max_blocks = s.max_blocks; r.max_seg = s.max_seg;
-  r.max_ws = w.max_ws;
-  r.logits = a.router_logits;
-  r.x = a.hidden_states;
-  r.gate_w = a.shared_gate_weight;
-  if (a.router_logits) {
-    r.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
-    r.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
-  } else {
-    r.topk_w = const_cast<float*>(a.topk_weights);
-    r.topk_ids = const_cast<int32_t*>(a.topk_ids);
-  }
-  r.gate = reinterpret_cast<float*>(ws + w.gate);
-  r.sorted = sorted; r.eids = eids; r.ntpp = ntpp; r.segs = segs; r.nseg = nseg;
-  r.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
-  r.nws = reinterpret_cast<int32_t*>(ws + w.nws);
-  r.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);
-  r.done = reinterpret_cast<int32_t*>(ws + w.done);
-  r.blobs = a.expert_blobs; r.expert_bytes = a.expert_bytes;
-  r.slot_table = a.slot_table; r.host_blobs = a.host_blobs; r.shared_blob = a.shared_blob;
-  r.status = status;
-  r.demand_log = a.demand_log;
-
   FusedArgs f;
   f.M = M; f.H = H; f.I = I; f.E = E; f.k = k; f.numel = numel; f.zero_mode = a.zero_mode;
-  f.has_shared = r.has_shared; f.G = G;
-  f.x = a.hidden_states; f.topk_w = r.topk_w; f.topk_ids = r.topk_ids;
-  f.wseg = r.wseg; f.nws = r.nws;
+  f.has_shared = a.shared_blob ? 1 : 0; f.G = G; f.renorm = a.renormalize ? 1 : 0;
+  f.max_ws = w.max_ws;
+  f.x = a.hidden_states;
+  f.logits = a.router_logits;
+  f.gate_w = a.shared_gate_weight;
+  if (a.router_logits) {
+    f.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
+    f.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
+  } else {
+    f.topk_w = const_cast<float*>(a.topk_weights);
+    f.topk_ids = const_cast<int32_t*>(a.topk_ids);
+  }
+  f.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
   f.L = L;
-  f.gate = r.gate; f.seg_done = r.seg_done; f.done = r.done;
+  f.blobs = a.expert_blobs; f.expert_bytes = a.expert_bytes;
+  f.slot_table = a.slot_table; f.host_blobs = a.host_blobs; f.shared_blob = a.shared_blob;
+  f.gate = reinterpret_cast<float*>(ws + w.gate);
+  f.bar = reinterpret_cast<int32_t*>(ws + w.bar);
+  f.cnt = reinterpret_cast<int32_t*>(ws + w.cnt);
+  f.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);
+  f.lists = reinterpret_cast<int32_t*>(ws + w.lists);
   f.hbuf = reinterpret_cast<uint16_t*>(ws + w.hbuf);
   f.ybuf = reinterpret_cast<float*>(ws + w.ybuf);
   f.out = a.out; f.out_f32 = a.out_f32;
-  f.status = status;
+  f.status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
+  f.demand_log = a.demand_log;
   f.stages = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
-  return launch_moe_fused(f, r, st);
+  return launch_moe_fused(f, st);
 }
 
 }  // extern "C"

@@ -17,51 +17,33 @@ constexpr int kWsInts = 4 + 8 * kWsBlocks;
 
 // Device-side arguments of the fused layer kernel (moe_fused.cu).
 struct FusedArgs {
-  int M, H, I, E, k, numel, zero_mode, has_shared, G;
+  int M, H, I, E, k, numel, zero_mode, has_shared, G, renorm, max_ws;
   const uint16_t* x;
-  const float* topk_w;
-  const int32_t* topk_ids;
-  const int32_t* wseg;       // [max_ws][kWsInts]
-  const int32_t* nws;        // [1]
+  const float* logits;       // [M, E] or NULL (topk_w / topk_ids given)
+  const uint16_t* gate_w;    // [H] shared-expert gate or NULL
+  float* topk_w;             // [M*k] written when logits != NULL
+  int32_t* topk_ids;         // [M*k]
+  int32_t* wseg;             // [max_ws][kWsInts] spill area for large ranges
   MtpExpertLayout L;
-  const float* gate;         // [M] sigmoid(x . w_g)
-  int32_t* seg_done;         // [max_ws] W1 units published per work segment
-  int32_t* done;             // [1] CTAs finished with W2
-  uint16_t* hbuf;
-  float* ybuf;
-  uint16_t* out;
-  float* out_f32;
-  int32_t* status;
-  int stages;
-  uint32_t stage_bytes;
-  uint32_t xbuf_bytes;
-};
-
-// Arguments of the route kernel that precedes it.
-struct RouteArgs {
-  int M, H, E, k, renorm, has_shared, numel, cap, max_blocks, max_seg, max_ws;
-  const float* logits;       // or NULL (use the given topk_w / topk_ids)
-  const uint16_t* x;
-  const uint16_t* gate_w;
-  float* topk_w;
-  int32_t* topk_ids;
-  float* gate;
-  int32_t* sorted;
-  int32_t* eids;
-  int32_t* ntpp;
-  int32_t* segs;
-  int32_t* nseg;
-  int32_t* wseg;
-  int32_t* nws;
-  int32_t* seg_done;
-  int32_t* done;
   const uint8_t* blobs;
   int64_t expert_bytes;
   const int32_t* slot_table;
   const uint8_t* host_blobs;
   const uint8_t* shared_blob;
+  float* gate;               // [M] sigmoid(x . w_g)
+  int32_t* bar;              // [2] grid barrier (count, generation)    \ zero before the first
+  int32_t* cnt;              // [E] pairs per expert                    |  call; every call
+  int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero
+  int32_t* lists;            // [E][M] pair ids per expert
+  uint16_t* hbuf;
+  float* ybuf;
+  uint16_t* out;
+  float* out_f32;
   int32_t* status;
   int32_t* demand_log;
+  int stages;
+  uint32_t stage_bytes;
+  uint32_t xbuf_bytes;
 };
 
 int launch_router_topk(const float* logits, int M, int E, int k, int renorm, float* w,
@@ -78,6 +60,6 @@ int gptq_dequant(const int32_t* q, const int32_t* z, const uint16_t* s, const in
 
 bool fused_supported(int H, int I, int G);
 int fused_max_work_segments(int M, int max_seg, int max_blocks);
-int launch_moe_fused(const FusedArgs& a, const RouteArgs& r, cudaStream_t st);
+int launch_moe_fused(const FusedArgs& a, cudaStream_t st);
 
 }  // namespace mtp

@@ -1,14 +1,18 @@
-// The W4A16 MoE layer forward on sm_100a as two kernels:
+// The W4A16 MoE layer forward on sm_100a as one persistent kernel (one CTA
+// per SM, 18 warps). It runs in three phases separated by grid-wide barriers:
 //
-//   route  (1 CTA, 1024 threads): router softmax/top-k/renormalise, the shared
-//          expert's sigmoid gate, moe_align (block 8), and the work-segment
-//          table the fused kernel runs on: each entry is one token block of
-//          one expert with its blob address already resolved through the slot
-//          table and its 8 pair ids inline. Resets the fused kernel's
-//          counters. Triggers programmatic dependent launch first thing so the
-//          fused kernel's CTAs are resident and waiting when it ends.
-//
-//   fused  (persistent: one CTA per SM, 18 warps, warp-specialised):
+//   routing  CTA c routes tokens c, c + G, ... (G = CTAs): router softmax /
+//            top-k / renormalise (warps 0-7, one token each), the shared
+//            expert's sigmoid gate (warps 8-15); each (token, slot) pair is
+//            appended to its expert's list with an atomic counter. Pair order
+//            inside a list does not change any result: every pair is its own
+//            MMA column.
+//   table    every CTA derives the work segments (the shared expert's token
+//            blocks, then each routed expert's pairs in blocks of 8, experts
+//            ascending) from the per-expert counts, and fills the entries of
+//            its own unit ranges into shared memory with the blob address
+//            already resolved through the slot table.
+//   experts  warp-specialised over the work units:
 //          warp 16  weight producer - streams each work unit's packed int4
 //                   strips, fp16 scales and zero nibbles from HBM into a ring
 //                   of shared-memory stages with 1-D bulk copies
@@ -18,10 +22,13 @@
 //                   block (8 x rows for W1, 8 h rows for W2) into a double
 //                   buffer; before the first W2 unit of a segment it waits
 //                   until all W1 units of that segment have published h;
-//          warps 0-15 consumers - dequantise int4 in registers (exponent
-//                   bias, exact q - z in bf16), m16n8k16 bf16 MMA with fp32
-//                   accumulation, per-chunk fp32 scale fold, cross-warp
-//                   reduction, then the epilogue.
+//          warps 0-15 consumers - quantise each new block of operand rows
+//                   in shared memory to 16-bit integers (a signed high-byte
+//                   row, an unsigned low-byte row, one scale per row), unpack
+//                   the int4 weights to u8, run exact int32 m16n8k32 MMAs
+//                   (u8 x s8 and u8 x u8) per quantisation group, fold the
+//                   zero point and the scales in fp32, reduce across warps,
+//                   then the epilogue.
 //
 // Work units, in this order (each CTA takes a contiguous range of each list;
 // a work segment is one token block, so ranges balance and every unit of a
@@ -33,8 +40,8 @@
 //   W2 unit (segment, row octet r): down rows 128r..128r+127 over K = I ->
 //      y = h . W2^T times the router weight (MUL_ROUTED_WEIGHT, :19761-19782),
 //      fp32 per pair.
-// Then one grid-wide arrival; after the last CTA arrives every CTA combines a
-// slice of the output: out = sum over the top-k slots in slot order of y +
+// Then a second grid-wide barrier, after which every CTA combines a slice of
+// the output and clears a slice of the per-call counters: out = sum over the top-k slots in slot order of y +
 // sigmoid(x . w_g) * y_shared (moe_sum :19801 and the shared-expert gate
 // :3994-4031, :4140-4152), so the result is deterministic.
 //
@@ -45,8 +52,9 @@
 // wait on later units and the final barrier is reached by every CTA after
 // its own units, so with all CTAs resident (one per SM, sized by shared
 // memory) nothing deadlocks. Every wait is bounded by a deadline on the
-// global timer; on expiry the kernel records bit 1 in status[2] and carries
-// on, so it always terminates.
+// global timer; on expiry the kernel sets bit 0 (value 1) of status[2] and
+// carries on, so it always terminates. A caller-given top-k row that repeats
+// an expert sets value 4 (the repeat is dropped).
 #include "internal.cuh"
 #include "route.cuh"
 
@@ -78,6 +86,9 @@ struct Ctrl {
   int stage_valid[kMaxStages];
   int seg_first[2];   // first work segment of the pass range
   int cached[2];      // 1 if the pass range's segments are in the table
+  int S;              // work segments of this call
+  int gen0;           // grid-barrier generation when the kernel started
+  int scan[32];       // block-scan scratch
 };
 static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
 
@@ -108,7 +119,7 @@ __device__ __forceinline__ void unit_range(int total_units, int& b, int& e) {
 
 __device__ __forceinline__ Pass make_pass(const FusedArgs& a, const Ctrl& cb, const int* table, int pass) {
   Pass P;
-  const int S = *a.nws;
+  const int S = cb.S;
   P.per = pass == 0 ? a.I / 16 : a.H / 128;
   unit_range(S * P.per, P.ub, P.ue);
   P.seg_first = cb.seg_first[pass];
@@ -125,6 +136,298 @@ __device__ __forceinline__ bool reuses_operand(const Pass& P, int u) {
 }
 
 __device__ __forceinline__ void record_timeout(const FusedArgs& a) { atomicOr(a.status + 2, 1); }
+
+// Grid-wide barrier over the kernel's CTAs (all resident: one per SM). One
+// thread per CTA calls it; the generation word a.bar[1] counts completed
+// barriers, so the kernel waits for `target` = its start value + n. The last
+// arriver clears the arrival count before it publishes the new generation, so
+// the count is zero again for the next barrier and the next call.
+__device__ __forceinline__ bool grid_sync(const FusedArgs& a, int target, uint64_t deadline) {
+  __threadfence();
+  const int old = atomicAdd(a.bar, 1);
+  if (old == static_cast<int>(gridDim.x) - 1) {
+    atomicExch(a.bar, 0);
+    __threadfence();
+    red_release_gpu_add(a.bar + 1, 1);
+    return true;
+  }
+  while (static_cast<int>(static_cast<uint32_t>(ld_acquire_gpu(a.bar + 1)) - static_cast<uint32_t>(target)) < 0) {
+    if (global_timer_ns() > deadline) return false;
+  }
+  return true;
+}
+
+// Exclusive scan over all threads of the CTA (blockDim.x <= 1024); `tmp` is
+// 32 ints of shared memory. Every thread must call it.
+__device__ __forceinline__ int cta_exclusive_scan(int v, int* total, int* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < nw ? tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, t, o);
+      if (lane >= o) t += y;
+    }
+    tmp[lane] = t;
+  }
+  __syncthreads();
+  const int base = warp > 0 ? tmp[warp - 1] : 0;
+  *total = tmp[nw - 1];
+  __syncthreads();
+  return base + x - v;
+}
+
+// ---------------------------------------------------------------------------
+// routing, spread over the CTAs: CTA c takes tokens c, c + G, c + 2G, ...
+// ---------------------------------------------------------------------------
+// Router for one token by one warp, E <= 1024 logits staged in shared memory:
+// softmax over all E, top-k descending with exact ties to the lower expert
+// id, optional renormalisation with the sum clamped to 1e-20 (vLLM
+// topk_softmax as tracing/vllm_router_trace.py:4201-4227 restates it). Lane
+// j < k returns pick j.
+__device__ __forceinline__ void router_warp(const float* __restrict__ row, int E, int k, int renorm, float* v,
+                                            float* w_out, int* id_out) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+  for (int base = 0; base < E; base += 256) {  // eight loads per lane in flight
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + 32 * j + lane;
+      x[j] = i < E ? row[i] : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + 32 * j + lane;
+      if (i < E) v[i] = x[j];
+      mx = fmaxf(mx, x[j]);
+    }
+  }
+  mx = warp_max(mx);
+  float s = 0.f;
+  for (int i = lane; i < E; i += 32) s += expf(v[i] - mx);
+  s = warp_sum(s);
+  // each lane's best untaken candidate (ascending id within the lane breaks ties)
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lane; i < E; i += 32)
+    if (v[i] > bv) {
+      bv = v[i];
+      bi = i;
+    }
+  float my_w = 0.f, wsum = 0.f;
+  int my_id = 0;
+  for (int j = 0; j < k; ++j) {
+    float wv = bv;
+    int wi = bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kFullMask, wv, o);
+      const int oi = __shfl_xor_sync(kFullMask, wi, o);
+      if (ov > wv || (ov == wv && oi < wi)) {
+        wv = ov;
+        wi = oi;
+      }
+    }
+    const float p = expf(wv - mx) / s;
+    wsum += p;
+    if (lane == j) {
+      my_w = p;
+      my_id = wi;
+    }
+    if (wi < E && (wi & 31) == lane) {  // the winner's lane takes it and rescans its column
+      v[wi] = -INFINITY;
+      bv = -INFINITY;
+      bi = 0x7fffffff;
+      for (int i = lane; i < E; i += 32)
+        if (v[i] > bv) {
+          bv = v[i];
+          bi = i;
+        }
+    }
+    __syncwarp();
+  }
+  if (renorm) my_w = my_w / fmaxf(wsum, 1e-20f);
+  *w_out = my_w;
+  *id_out = my_id;
+}
+
+// Phase 1 (consumer warps): route this CTA's tokens, count and list the
+// (token, slot) pairs per expert, and compute the shared-expert gate. Warps
+// 0-7 route a token each; warps 8-15 compute the gates of the same tokens.
+// `scratch` holds 8 x E floats (the stage ring, still unused).
+__device__ void route_phase(const FusedArgs& a, int ctid, float* scratch) {
+  const int warp = ctid >> 5, lane = ctid & 31;
+  const int G = gridDim.x;
+  for (int i0 = 0; static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * i0 < a.M; i0 += 8) {
+    const int64_t t64 = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * (i0 + (warp & 7));
+    if (t64 >= a.M) continue;
+    const int t = static_cast<int>(t64);
+    if (warp < 8) {
+      int id = -1;
+      if (a.logits) {
+        float w;
+        router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + warp * a.E, &w, &id);
+        if (lane < a.k) {
+          a.topk_w[t * a.k + lane] = w;
+          a.topk_ids[t * a.k + lane] = id;
+        }
+      } else if (lane < a.k) {
+        id = a.topk_ids[t * a.k + lane];
+      }
+      if (lane < a.k && id >= 0 && id < a.E) {
+        // an expert holds at most one pair per token (distinct ids per token);
+        // a repeated id in a caller-given row is dropped and flagged
+        const int pos = atomicAdd(a.cnt + id, 1);
+        if (pos < a.M) a.lists[static_cast<int64_t>(id) * a.M + pos] = t * a.k + lane;
+        else atomicOr(a.status + 2, 4);
+      }
+    } else if (a.has_shared) {
+      // sigmoid(x . w_g): all of a lane's 16-byte loads in flight at once
+      const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(t) * a.H);
+      const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
+      const int nvec = a.H / 8;  // <= 256: at most 8 per lane
+      uint4 xv[8], wv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int vi = lane + 32 * j;
+        if (vi < nvec) {
+          xv[j] = xr[vi];
+          wv[j] = wg[vi];
+        }
+      }
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (lane + 32 * j < nvec) {
+          const uint32_t* xs = reinterpret_cast<const uint32_t*>(&xv[j]);
+          const uint32_t* ws = reinterpret_cast<const uint32_t*>(&wv[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            part = fmaf(__uint_as_float(xs[q] << 16), __uint_as_float(ws[q] << 16), part);
+            part = fmaf(__uint_as_float(xs[q] & 0xffff0000u), __uint_as_float(ws[q] & 0xffff0000u), part);
+          }
+        }
+      }
+      part = warp_sum(part);
+      if (lane == 0) a.gate[t] = 1.f / (1.f + expf(-part));
+    }
+  }
+}
+
+// Work segment s as a table entry (see kWsInts): the shared expert's token
+// blocks first, then every routed expert in ascending id, cut into blocks of
+// kFBM pairs. `cnt` / `sbase` are the per-expert pair counts and exclusive
+// segment offsets in shared memory.
+__device__ void fill_entry(const FusedArgs& a, int s, int shared_ws, const int* cnt, const int* sbase, int* w) {
+  const uint8_t* blob = nullptr;
+  int flags = 0;
+  if (s < shared_ws) {
+    blob = a.shared_blob;
+    flags = 1;
+    for (int j = 0; j < kFBM; ++j) {
+      const int tk = s * kFBM + j;
+      w[4 + j] = tk < a.M ? a.numel + tk : -1;
+    }
+  } else {
+    const int r = s - shared_ws;
+    int lo = 0, hi = a.E - 1;  // last expert with sbase <= r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sbase[mid] <= r) lo = mid; else hi = mid - 1;
+    }
+    const int ex = lo, b = r - sbase[ex];
+    for (int j = 0; j < kFBM; ++j) {
+      const int idx = b * kFBM + j;
+      w[4 + j] = idx < cnt[ex] ? __ldcg(a.lists + static_cast<int64_t>(ex) * a.M + idx) : -1;
+    }
+    const int slot = a.slot_table ? a.slot_table[ex] : ex;
+    if (slot >= 0) {
+      blob = a.blobs + static_cast<int64_t>(slot) * a.expert_bytes;
+    } else if (a.host_blobs) {
+      blob = a.host_blobs + static_cast<int64_t>(ex) * a.expert_bytes;
+      flags = 2;
+    }
+  }
+  const uint64_t addr = reinterpret_cast<uint64_t>(blob);
+  w[0] = static_cast<int32_t>(addr & 0xffffffffu);
+  w[1] = static_cast<int32_t>(addr >> 32);
+  w[2] = 1;
+  w[3] = flags;
+}
+
+// Phase 2 (all threads, after the grid barrier): every CTA derives the work
+// segments from the per-expert counts and fills the table entries of its own
+// two unit ranges; CTA 0 also writes the demand log and the miss counts.
+// `scratch` holds 2E + 1 ints (the operand buffers, still unused).
+__device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scratch) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  int* cnt = scratch;           // [E]
+  int* sbase = scratch + a.E;   // [E + 1]
+  // each thread owns experts [2 tid, 2 tid + 2) (E <= 1024 < 2 * 576)
+  int c0 = 0, c1 = 0;
+  if (2 * tid < a.E) c0 = min(__ldcg(a.cnt + 2 * tid), a.M);
+  if (2 * tid + 1 < a.E) c1 = min(__ldcg(a.cnt + 2 * tid + 1), a.M);
+  const int n0 = (c0 + kFBM - 1) / kFBM, n1 = (c1 + kFBM - 1) / kFBM;
+  int total;
+  const int ex = cta_exclusive_scan(n0 + n1, &total, cb.scan);
+  if (2 * tid < a.E) {
+    cnt[2 * tid] = c0;
+    sbase[2 * tid] = ex;
+  }
+  if (2 * tid + 1 < a.E) {
+    cnt[2 * tid + 1] = c1;
+    sbase[2 * tid + 1] = ex + n0;
+  }
+  if (tid == 0) sbase[a.E] = total;
+  const int shared_ws = a.has_shared ? (a.M + kFBM - 1) / kFBM : 0;
+  const int S = shared_ws + total;
+  if (tid == 0) cb.S = S;
+  if (blockIdx.x == 0) {
+    const int u0 = c0 > 0, u1 = c1 > 0;
+    int nused;
+    const int rank = cta_exclusive_scan(u0 + u1, &nused, cb.scan);
+    if (a.demand_log) {
+      if (tid == 0) a.demand_log[0] = nused;
+      if (u0) a.demand_log[1 + rank] = 2 * tid;
+      if (u1) a.demand_log[1 + rank + u0] = 2 * tid + 1;
+    }
+    for (int j = 0; j < 2; ++j) {
+      const int e = 2 * tid + j;
+      if (e < a.E && (j == 0 ? u0 : u1)) {
+        const int slot = a.slot_table ? a.slot_table[e] : e;
+        if (slot < 0) atomicAdd(a.host_blobs ? a.status + 0 : a.status + 1, 1);
+      }
+    }
+  }
+  __syncthreads();
+  for (int pass = 0; pass < 2; ++pass) {
+    const int per = pass == 0 ? a.I / 16 : a.H / 128;
+    int ub, ue;
+    unit_range(S * per, ub, ue);
+    const int first = ub / per;
+    const int last = ue > ub ? (ue - 1) / per : first - 1;
+    const int n = last - first + 1;
+    const bool cached = n <= kWsCache;
+    if (tid == 0) {
+      cb.seg_first[pass] = first;
+      cb.cached[pass] = cached;
+    }
+    for (int i = tid; i < n; i += nt) {
+      int* w = cached ? table + (pass * kWsCache + i) * kWsInts : a.wseg + static_cast<size_t>(first + i) * kWsInts;
+      fill_entry(a, first + i, shared_ws, cnt, sbase, w);
+    }
+  }
+  __syncthreads();
+}
 
 __device__ __forceinline__ uint32_t lds8(uint32_t addr) {
   uint16_t v;
@@ -397,6 +700,7 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
   int st = 0, xb = 0;
   uint32_t ph = 0, xph = 0;
   const int ld_row = lane & 7, ld_mat = lane >> 3;  // ldmatrix row address of this lane
+  int published = 0;  // W1 units of the current segment not yet published
 
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
@@ -501,7 +805,13 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
           // protects red from the next unit and orders the h stores before the
           // release below
           named_bar_sync(kBarConsumers, kCT);
-          if (blk == nb - 1 && ctid == 0) red_release_gpu_add(a.seg_done + seg, 1);
+          // publish this CTA's h columns of the segment once, when it leaves
+          // the segment (or its range)
+          ++published;
+          if (blk == nb - 1 && (u + 1 == P.ue || (u + 1) / P.per != seg)) {
+            if (ctid == 0) red_release_gpu_add(a.seg_done + seg, published);
+            published = 0;
+          }
         } else {
           // ------------------------------ W2 ------------------------------
           const int sidx = warp >> 1, hk = warp & 1;
@@ -565,8 +875,8 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
           named_bar_sync(kBarConsumers, kCT);
           if (hk == 0) {
             const int p0 = cols[2 * t], p1 = cols[2 * t + 1];
-            const float w0 = ((p0 >= 0 && p0 < a.numel) ? a.topk_w[p0] : 1.f) * meta.sx[2 * t];
-            const float w1 = ((p1 >= 0 && p1 < a.numel) ? a.topk_w[p1] : 1.f) * meta.sx[2 * t + 1];
+            const float w0 = ((p0 >= 0 && p0 < a.numel) ? __ldcg(a.topk_w + p0) : 1.f) * meta.sx[2 * t];
+            const float w1 = ((p1 >= 0 && p1 < a.numel) ? __ldcg(a.topk_w + p1) : 1.f) * meta.sx[2 * t + 1];
             const int nbase = 128 * idx + 16 * sidx;
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -597,18 +907,15 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
 
   // ------------------------- grid arrival + combine -------------------------
   named_bar_sync(kBarConsumers, kCT);
-  if (ctid == 0) {
-    red_release_gpu_add(a.done, 1);
-    bool ok = true;
-    while (ld_acquire_gpu(a.done) < static_cast<int>(gridDim.x)) {
-      if (global_timer_ns() > deadline) {
-        ok = false;
-        break;
-      }
-    }
-    if (!ok) record_timeout(a);
-  }
+  if (ctid == 0 && !grid_sync(a, cb.gen0 + 2, deadline)) record_timeout(a);
   named_bar_sync(kBarConsumers, kCT);
+  // The per-call counters are no longer read by anyone: zero them for the
+  // next call, a slice per CTA.
+  {
+    const int G = gridDim.x, c = blockIdx.x;
+    for (int i = a.E * c / G + ctid; i < a.E * (c + 1) / G; i += kCT) a.cnt[i] = 0;
+    for (int i = cb.S * c / G + ctid; i < cb.S * (c + 1) / G; i += kCT) a.seg_done[i] = 0;
+  }
   const int quads = a.H / 4;
   const int64_t total = static_cast<int64_t>(a.M) * quads;
   const int64_t b = total * blockIdx.x / gridDim.x, e = total * (blockIdx.x + 1) / gridDim.x;
@@ -618,7 +925,7 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
     float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < a.k; ++j) {
       const int pp = tok * a.k + j;
-      const int ex = a.topk_ids[pp];
+      const int ex = __ldcg(a.topk_ids + pp);
       if (ex >= 0 && ex < a.E) {
         const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(pp) * a.H + n);
         sum.x += y.x;
@@ -628,7 +935,7 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
       }
     }
     if (a.has_shared) {
-      const float gt = a.gate[tok];
+      const float gt = __ldcg(a.gate + tok);
       const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(a.numel + tok) * a.H + n);
       sum.x = fmaf(gt, y.x, sum.x);
       sum.y = fmaf(gt, y.y, sum.y);
@@ -667,30 +974,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a
     }
     fence_mbar_init();
   }
-  // Everything below reads what the route kernel wrote.
-  pdl_wait();
+  if (threadIdx.x == 0) cb.gen0 = ld_acquire_gpu(a.bar + 1);
   const uint64_t deadline = global_timer_ns() + kTimeoutNs;
-  // Copy this CTA's two ranges of work segments into shared memory.
-  {
-    const int S = *a.nws;
-    for (int pass = 0; pass < 2; ++pass) {
-      const int per = pass == 0 ? a.I / 16 : a.H / 128;
-      int ub, ue;
-      unit_range(S * per, ub, ue);
-      const int first = ub / per;
-      const int last = ue > ub ? (ue - 1) / per : first - 1;
-      const int n = last - first + 1;
-      if (threadIdx.x == 0) {
-        cb.seg_first[pass] = first;
-        cb.cached[pass] = n <= kWsCache;
-      }
-      if (n > 0 && n <= kWsCache) {
-        const int4* src = reinterpret_cast<const int4*>(a.wseg + static_cast<size_t>(first) * kWsInts);
-        int4* dst = reinterpret_cast<int4*>(table + pass * kWsCache * kWsInts);
-        for (int i = threadIdx.x; i < n * kWsInts / 4; i += kFusedThreads) dst[i] = src[i];
-      }
-    }
-  }
+  __syncthreads();
+  // Phase 1: route this CTA's tokens (the stage ring is free scratch).
+  if (warp < kCW) route_phase(a, threadIdx.x, reinterpret_cast<float*>(stages));
+  __syncthreads();
+  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 1, deadline)) record_timeout(a);
+  __syncthreads();
+  // Phase 2: the work-segment table of this CTA's unit ranges.
+  build_table(a, cb, table, reinterpret_cast<int*>(stages));
   __syncthreads();
   if (warp == kWProd) {
     weight_producer(a, cb, table, stages, deadline);
@@ -698,150 +991,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a
     operand_producer(a, cb, table, xbufs, deadline);
   } else {
     consumers<W1C, W2C>(a, cb, table, stages, xbufs, metas, red, deadline);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// route kernel
-// ---------------------------------------------------------------------------
-template <int VPT>
-__global__ void __launch_bounds__(kAlignThreads) moe_route_kernel(RouteArgs r) {
-  pdl_launch_dependents();
-  extern __shared__ int sm[];
-  __shared__ int scan_tmp[32];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) *r.done = 0;
-  for (int i = tid; i < r.max_ws; i += kAlignThreads) r.seg_done[i] = 0;
-  for (int tkn = warp; tkn < r.M; tkn += kAlignThreads / 32) {
-    if (r.logits) {
-      float w;
-      int id;
-      router_token<VPT>(r.logits + static_cast<int64_t>(tkn) * r.E, r.E, r.k, r.renorm, &w, &id);
-      if (lane < r.k) {
-        r.topk_w[tkn * r.k + lane] = w;
-        r.topk_ids[tkn * r.k + lane] = id;
-      }
-    }
-    if (r.has_shared) {
-      // sigmoid(x . w_g): 8 bf16 per 16-byte load, loads issued 2 at a time
-      // (the 1024-thread block leaves 64 registers a thread)
-      const uint4* xr = reinterpret_cast<const uint4*>(r.x + static_cast<int64_t>(tkn) * r.H);
-      const uint4* wg = reinterpret_cast<const uint4*>(r.gate_w);
-      float part = 0.f;
-      const int nvec = r.H / 8;
-      for (int v0 = lane; v0 < nvec; v0 += 32 * 2) {
-        uint4 xv[2], wv[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int v = v0 + 32 * j;
-          if (v < nvec) {
-            xv[j] = xr[v];
-            wv[j] = wg[v];
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int v = v0 + 32 * j;
-          if (v < nvec) {
-            const uint32_t* xs = reinterpret_cast<const uint32_t*>(&xv[j]);
-            const uint32_t* ws = reinterpret_cast<const uint32_t*>(&wv[j]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              part = fmaf(__uint_as_float(xs[q] << 16), __uint_as_float(ws[q] << 16), part);
-              part = fmaf(__uint_as_float(xs[q] & 0xffff0000u), __uint_as_float(ws[q] & 0xffff0000u), part);
-            }
-          }
-        }
-      }
-      part = warp_sum(part);
-      if (lane == 0) r.gate[tkn] = 1.f / (1.f + expf(-part));
-    }
-  }
-  __syncthreads();
-  align_block(r.topk_ids, r.numel, r.E, kFBM, nullptr, 0, r.cap, r.max_blocks, r.max_seg, r.sorted, r.eids,
-              r.ntpp, r.segs, r.nseg, sm, scan_tmp);
-  __syncthreads();
-
-  // Work segments: the shared expert first, then each routed expert, every
-  // one cut into pieces of kWsBlocks token block(s).
-  const int nseg = *r.nseg;
-  const int shared_blocks = r.has_shared ? (r.M + kFBM - 1) / kFBM : 0;
-  const int shared_ws = (shared_blocks + kWsBlocks - 1) / kWsBlocks;
-  int mine = 0;  // work segments of routed segment tid
-  int e = -1, b0 = 0, nb = 0;
-  if (tid < nseg) {
-    e = r.segs[3 * tid];
-    b0 = r.segs[3 * tid + 1];
-    nb = r.segs[3 * tid + 2];
-    mine = (nb + kWsBlocks - 1) / kWsBlocks;
-  }
-  int total;
-  const int first = shared_ws + block_exclusive_scan(mine, &total, scan_tmp);
-  if (tid == 0) *r.nws = shared_ws + total;
-  // segment -> (first work segment, expert, blocks) for the warp-parallel fill
-  int* ws_first = sm;                 // [nseg] (align scratch is free now)
-  if (tid < nseg) ws_first[tid] = first;
-  if (tid < nseg) {
-    const int slot = r.slot_table ? r.slot_table[e] : e;
-    if (slot < 0) atomicAdd(r.host_blobs ? r.status + 0 : r.status + 1, 1);
-  }
-  __syncthreads();
-  const int nws = shared_ws + total;
-  for (int wsi = warp; wsi < nws; wsi += kAlignThreads / 32) {
-    int32_t* w = r.wseg + static_cast<size_t>(wsi) * kWsInts;
-    const uint8_t* blob = nullptr;
-    int flags = 0, cnt = 0, base = 0;
-    bool shared = wsi < shared_ws;
-    int seg = -1;
-    if (shared) {
-      blob = r.shared_blob;
-      flags = 1;
-      cnt = min(kWsBlocks, shared_blocks - wsi * kWsBlocks);
-      base = wsi * kWsBlocks * kFBM;  // first token
-    } else {
-      // the routed segment whose range holds wsi (ws_first ascending)
-      int lo = 0, hi = nseg - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (ws_first[mid] <= wsi) lo = mid; else hi = mid - 1;
-      }
-      seg = lo;
-      const int ex = r.segs[3 * seg], sb0 = r.segs[3 * seg + 1], snb = r.segs[3 * seg + 2];
-      const int q = wsi - ws_first[seg];
-      cnt = min(kWsBlocks, snb - q * kWsBlocks);
-      base = (sb0 + q * kWsBlocks) * kFBM;
-      const int slot = r.slot_table ? r.slot_table[ex] : ex;
-      if (slot >= 0) {
-        blob = r.blobs + static_cast<int64_t>(slot) * r.expert_bytes;
-      } else if (r.host_blobs) {
-        blob = r.host_blobs + static_cast<int64_t>(ex) * r.expert_bytes;
-        flags = 2;
-      }
-    }
-    if (lane < kWsBlocks * kFBM) {
-      int p = -1;
-      if (lane < cnt * kFBM) {
-        if (shared) {
-          const int tk = base + lane;
-          p = tk < r.M ? r.numel + tk : -1;
-        } else {
-          p = r.sorted[base + lane];
-          p = (p >= 0 && p < r.numel) ? p : -1;
-        }
-      }
-      w[4 + lane] = p;
-    }
-    if (lane == 0) {
-      const uint64_t addr = reinterpret_cast<uint64_t>(blob);
-      w[0] = static_cast<int32_t>(addr & 0xffffffffu);
-      w[1] = static_cast<int32_t>(addr >> 32);
-      w[2] = cnt;
-      w[3] = flags;
-    }
-  }
-  if (r.demand_log) {
-    if (tid == 0) r.demand_log[0] = nseg;
-    for (int i = tid; i < nseg; i += kAlignThreads) r.demand_log[1 + i] = r.segs[3 * i];
   }
 }
 
@@ -901,11 +1050,8 @@ static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream
   cfg.blockDim = dim3(kFusedThreads);
   cfg.dynamicSmemBytes = f.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
   if (cudaLaunchKernelEx(&cfg, moe_fused_kernel<W1C, W2C>, a) != cudaSuccess) return MTP_ERR_LAUNCH;
   return MTP_OK;
 }
@@ -931,39 +1077,12 @@ int fused_max_work_segments(int M, int max_seg, int max_blocks) {
   return max_seg + max_blocks / kWsBlocks + (shared_blocks + kWsBlocks - 1) / kWsBlocks + 2;
 }
 
-int launch_moe_fused(const FusedArgs& a_in, const RouteArgs& r, cudaStream_t st) {
+int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {
   FusedArgs a = a_in;
   const FusedGeometry f = fused_geometry(a.H, a.I, a.G);
   a.stages = f.stages;
   a.stage_bytes = f.stage_bytes;
   a.xbuf_bytes = f.xbuf_bytes;
-  {
-    static int configured = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int sm = static_cast<int>(align_smem_bytes(1024));
-    if (configured != dev) {
-      const bool ok =
-          cudaFuncSetAttribute(moe_route_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
-          cudaFuncSetAttribute(moe_route_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
-          cudaFuncSetAttribute(moe_route_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
-          cudaFuncSetAttribute(moe_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
-          cudaFuncSetAttribute(moe_route_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess &&
-          cudaFuncSetAttribute(moe_route_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) == cudaSuccess;
-      if (!ok) return MTP_ERR_CUDA;
-      configured = dev;
-    }
-    const size_t smem = align_smem_bytes(r.E);
-    const int vpt = (r.E + 31) / 32;
-    if (vpt <= 1) moe_route_kernel<1><<<1, kAlignThreads, smem, st>>>(r);
-    else if (vpt <= 2) moe_route_kernel<2><<<1, kAlignThreads, smem, st>>>(r);
-    else if (vpt <= 4) moe_route_kernel<4><<<1, kAlignThreads, smem, st>>>(r);
-    else if (vpt <= 8) moe_route_kernel<8><<<1, kAlignThreads, smem, st>>>(r);
-    else if (vpt <= 16) moe_route_kernel<16><<<1, kAlignThreads, smem, st>>>(r);
-    else moe_route_kernel<32><<<1, kAlignThreads, smem, st>>>(r);
-    const int rs = launch_status();
-    if (rs != MTP_OK) return rs;
-  }
   int w1c, w2c;
   fused_template(a.H, a.I, &w1c, &w2c);
 #define MTP_FUSED_CASE(A, B) \

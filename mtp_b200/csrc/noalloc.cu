@@ -10,7 +10,7 @@
 // array compiled into the library instead.
 //
 // The scratch is a file-scope __device__ array of kNoAllocScratchBytes
-// (4 MiB, enough for M <= 48 tokens at H = 2048, I = 512, E = 256, top-8);
+// (5 MiB, enough for M <= 48 tokens at H = 2048, I = 512, E = 256, top-8);
 // every GPU that loads the library holds it until the process exits. Larger
 // requests are rejected with MTP_ERR_WORKSPACE before anything is launched.
 //
@@ -18,9 +18,10 @@
 // address is looked up with cudaGetSymbolAddress, once per device, with that
 // device current, on the first call made on that device; that first call
 // should therefore come before any stream capture. All calls share the one
-// array and it keeps the last call's contents: the layer's route kernel clears
-// the counters that must start at zero on every call, and everything else is
-// written before it is read. Calls that overlap on the GPU (other streams,
+// array and it keeps the last call's contents: the counters that must start
+// at zero are zero when the library loads (a __device__ array starts zeroed)
+// and every completed call leaves them zero again; everything else is written
+// before it is read. Calls that overlap on the GPU (other streams,
 // other host threads) race on the array and must be serialised by the caller.
 //
 // Nothing here allocates: no cudaMalloc, no cudaFree, no allocating library

@@ -202,7 +202,9 @@ class SharedExpert:
 # ---------------------------------------------------------------------------
 def layer_workspace(m: int, experts: W4A16Experts, top_k: int, device) -> torch.Tensor:
     nbytes = _lib.layer_workspace_bytes(m, experts.num_experts, top_k, experts.hidden, experts.inter)
-    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    # zero-filled once: the layer keeps its call counters there and leaves
+    # them zero after every call
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
 
 def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | None,
