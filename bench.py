@@ -271,10 +271,16 @@ def run_gpu(args, rank: int, world: int):
     total_bytes = sum(bytes_per_m.values())
     total_ms = sum(per_m_ms.values())
     achieved = total_bytes / (total_ms / 1e3) / 1e9
+    # DRAM traffic per launch: the ncu-measured traffic/algorithmic ratio of
+    # the layer kernel (profiles/traffic.json, one capture at M=16) applied to
+    # this run's average algorithmic bytes per launch
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
+    n_launch = len(sweep) * args.layers
     if tp.exists():
-        traffic = json.loads(tp.read_text()).get("layer_step_bytes")
+        ratio = json.loads(tp.read_text()).get("traffic_over_algorithmic")
+        if ratio:
+            traffic = round(ratio * total_bytes / n_launch)
 
     # end to end through the public API with host buffers (pinned), copies timed
     e2e = run_e2e(args, layers, cfg, sweep, dev, state) if not args.no_e2e else None
@@ -288,11 +294,12 @@ def run_gpu(args, rank: int, world: int):
                    "tokens": sweep, "layers_per_graph": args.layers, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: L distinct layers (L x 418 MB) and fresh routing per call"},
         "sweep": rows,
-        "roofline": {"bound": "hbm", "kernel": "w4a16_moe_layer (router+align+W1+W2+combine), all sweep M",
+        "roofline": {"bound": "hbm", "kernel": "moe_fused_kernel (route+W1+W2+combine, one launch per layer), "
+                                               "bytes and time summed over the sweep",
                      "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
                      "frac": round(achieved / hbm_gbs, 4), "peak_source": peak_kind,
                      "traffic": traffic},
-        "gpu_launches": args.steps * len(sweep) * args.layers * 5,
+        "gpu_launches": args.steps * len(sweep) * args.layers,
         "clocks": clocks.summary(),
     }
     if e2e is not None:
