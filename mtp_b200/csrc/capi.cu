@@ -150,7 +150,7 @@ int mtp_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint16
 
 int mtp_w4a16_expert_layout(int32_t hidden, int32_t inter, int32_t group_size, MtpExpertLayout* out) {
   if (!out) return MTP_ERR_NULL;
-  if (hidden <= 0 || inter <= 0 || hidden % 64 || inter % 64 || group_size % 64 ||
+  if (hidden <= 0 || inter <= 0 || hidden % 128 || inter % 64 || group_size % 64 ||
       hidden % group_size || inter % group_size)
     return MTP_ERR_SHAPE;
   return expert_layout(hidden, inter, group_size, out);
@@ -241,7 +241,7 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   f.out = a.out; f.out_f32 = a.out_f32;
   f.status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
   f.demand_log = a.demand_log;
-  f.stages = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
+  f.stages = 0; f.sk = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
   return launch_moe_fused(f, st);
 }
 

@@ -7,18 +7,19 @@
 // 8j+i; scales [K/G, N] fp16.
 //
 // Kernel layout (this build's own; one expert = one contiguous blob so that a
-// slot fill is a single copy):
-//   weights  [N/16 strips][K/64 chunks][32 lanes][4 words]: the 16 bytes lane l
-//            reads for (strip s, chunk c) hold its A operands of the two
-//            m16n8k32 (8-bit) tiles covering rows 16s..16s+15, k 64c..64c+63.
-//            Word kk of lane l (g = l/4, t = l%4, row r = 16s + g + 8(kk&1),
-//            kb = 64c + 32(kk>>1)) holds, in byte b = 0..3, the nibble pair
-//            low = q(r, kb + 4t + b), high = q(r, kb + 16 + 4t + b),
-//            so `w & 0x0F0F0F0F` and `(w >> 4) & 0x0F0F0F0F` are the u8 A
-//            registers for k = kb+4t..+3 and kb+16+4t..+3 (see common.cuh).
-//   scales   [N/16][K/G][8][2] fp16: for (strip, group), lane group g reads one
-//            32-bit word = (scale of row g, scale of row g+8).
-//   zeros    [N/16][K/G][8] bytes: byte g = zero(row g) | zero(row g+8) << 4.
+// slot fill is a single copy). Each projection is cut into row blocks of 128
+// output rows, the M of one tensor-core MMA: for w13 (N = 2I) block b holds
+// gate rows 64b..64b+63 then up rows I+64b..I+64b+63, so one block yields
+// silu(gate) * up for 64 columns of h; for w2 block b holds rows 128b..+127.
+//   weights  [N/128 blocks][K/32 chunks][128 rows][16 bytes]: the 16 bytes of
+//            (block, chunk, row) hold k = 32c..32c+31 of that row as four
+//            32-bit words; word j covers k0 = 32c + 8j and holds, in byte
+//            t = 0..3, low nibble q(k0 + t) and high nibble q(k0 + 4 + t), so
+//            `w & 0x0F0F0F0F` and `(w >> 4) & 0x0F0F0F0F` are the u8 values
+//            of k0..k0+3 and k0+4..k0+7 in order (one tensor-memory column
+//            each). A K range of a block is one contiguous byte range.
+//   scales   [N/128][K/G][128] fp16.
+//   zeros    [N/128][K/G][64] bytes: byte i = zero(row 2i) | zero(row 2i+1) << 4.
 // Byte sizes equal the GPTQ ones (N*K/2, 2*N*K/G, N*K/(2G)).
 #include "internal.cuh"
 
@@ -54,31 +55,36 @@ __device__ __forceinline__ uint32_t gptq_nib_rows(const int32_t* q, int N, int k
   return (static_cast<uint32_t>(q[static_cast<int64_t>(k >> 3) * N + n]) >> ((k & 7) * 4)) & 0xFu;
 }
 
-__global__ void repack_qweight_kernel(const int32_t* __restrict__ gq, int N, int K, int E,
+// Source row (output channel) of row r of block b.
+__device__ __forceinline__ int block_row(int N, int gated, int b, int r) {
+  if (gated) return r < 64 ? 64 * b + r : N / 2 + 64 * b + (r - 64);
+  return 128 * b + r;
+}
+
+__global__ void repack_qweight_kernel(const int32_t* __restrict__ gq, int N, int K, int gated, int E,
                                       uint8_t* __restrict__ blobs, int64_t stride, int64_t off) {
   const int64_t words = static_cast<int64_t>(N) * K / 8;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (gid >= words * E) return;
   const int e = static_cast<int>(gid / words);
   const int64_t w = gid % words;
-  const int kk = static_cast<int>(w & 3);
-  const int l = static_cast<int>((w >> 2) & 31);
-  const int64_t rest = w >> 7;
-  const int chunks = K / 64;
-  const int c = static_cast<int>(rest % chunks);
-  const int s = static_cast<int>(rest / chunks);
-  const int g = l >> 2, t = l & 3;
-  const int r = 16 * s + g + 8 * (kk & 1);
-  const int kb = 64 * c + 32 * (kk >> 1) + 4 * t;
+  const int j = static_cast<int>(w & 3);
+  const int r = static_cast<int>((w >> 2) & 127);
+  const int64_t bc = w >> 9;
+  const int chunks = K / 32;
+  const int c = static_cast<int>(bc % chunks);
+  const int b = static_cast<int>(bc / chunks);
+  const int row = block_row(N, gated, b, r);
+  const int k0 = 32 * c + 8 * j;
   const int32_t* q = gq + static_cast<int64_t>(e) * (K / 8) * N;
   uint32_t word = 0;
 #pragma unroll
-  for (int b = 0; b < 4; ++b)
-    word |= (gptq_nib_rows(q, N, kb + b, r) | gptq_nib_rows(q, N, kb + 16 + b, r) << 4) << (8 * b);
+  for (int t = 0; t < 4; ++t)
+    word |= (gptq_nib_rows(q, N, k0 + t, row) | gptq_nib_rows(q, N, k0 + 4 + t, row) << 4) << (8 * t);
   reinterpret_cast<uint32_t*>(blobs + e * stride + off)[w] = word;
 }
 
-__global__ void repack_scales_kernel(const uint16_t* __restrict__ gs, int N, int K, int G, int E,
+__global__ void repack_scales_kernel(const uint16_t* __restrict__ gs, int N, int K, int G, int gated, int E,
                                      uint8_t* __restrict__ blobs, int64_t stride, int64_t off) {
   const int groups = K / G;
   const int64_t per = static_cast<int64_t>(N) * groups;
@@ -86,12 +92,11 @@ __global__ void repack_scales_kernel(const uint16_t* __restrict__ gs, int N, int
   if (gid >= per * E) return;
   const int e = static_cast<int>(gid / per);
   const int64_t i = gid % per;
-  const int h = static_cast<int>(i & 1);
-  const int g = static_cast<int>((i >> 1) & 7);
-  const int64_t sg = i >> 4;
-  const int grp = static_cast<int>(sg % groups);
-  const int s = static_cast<int>(sg / groups);
-  const int n = 16 * s + g + 8 * h;
+  const int r = static_cast<int>(i & 127);
+  const int64_t bg = i >> 7;
+  const int grp = static_cast<int>(bg % groups);
+  const int b = static_cast<int>(bg / groups);
+  const int n = block_row(N, gated, b, r);
   reinterpret_cast<uint16_t*>(blobs + e * stride + off)[i] =
       gs[static_cast<int64_t>(e) * groups * N + static_cast<int64_t>(grp) * N + n];
 }
@@ -101,7 +106,7 @@ __device__ __forceinline__ uint32_t gptq_nib_cols(const int32_t* z, int N, int g
          0xFu;
 }
 
-__global__ void repack_zeros_kernel(const int32_t* __restrict__ gz, int N, int K, int G, int E,
+__global__ void repack_zeros_kernel(const int32_t* __restrict__ gz, int N, int K, int G, int gated, int E,
                                     uint8_t* __restrict__ blobs, int64_t stride, int64_t off) {
   const int groups = K / G;
   const int64_t per = static_cast<int64_t>(N) * groups / 2;
@@ -109,25 +114,29 @@ __global__ void repack_zeros_kernel(const int32_t* __restrict__ gz, int N, int K
   if (gid >= per * E) return;
   const int e = static_cast<int>(gid / per);
   const int64_t i = gid % per;
-  const int g = static_cast<int>(i & 7);
-  const int64_t sg = i >> 3;
-  const int grp = static_cast<int>(sg % groups);
-  const int s = static_cast<int>(sg / groups);
+  const int rp = static_cast<int>(i & 63);
+  const int64_t bg = i >> 6;
+  const int grp = static_cast<int>(bg % groups);
+  const int b = static_cast<int>(bg / groups);
   const int32_t* z = gz + static_cast<int64_t>(e) * groups * (N / 8);
-  const uint32_t b = gptq_nib_cols(z, N, grp, 16 * s + g) | gptq_nib_cols(z, N, grp, 16 * s + g + 8) << 4;
-  (blobs + e * stride + off)[i] = static_cast<uint8_t>(b);
+  const uint32_t v = gptq_nib_cols(z, N, grp, block_row(N, gated, b, 2 * rp)) |
+                     gptq_nib_cols(z, N, grp, block_row(N, gated, b, 2 * rp + 1)) << 4;
+  (blobs + e * stride + off)[i] = static_cast<uint8_t>(v);
 }
 
 static int repack_proj(const int32_t* q, const int32_t* z, const uint16_t* s, int N, int K, int G,
-                       int E, uint8_t* blobs, int64_t stride, int64_t off_q, int64_t off_s,
+                       int gated, int E, uint8_t* blobs, int64_t stride, int64_t off_q, int64_t off_s,
                        int64_t off_z, cudaStream_t st) {
   const int T = 256;
   const int64_t nq = static_cast<int64_t>(N) * K / 8 * E;
   const int64_t ns = static_cast<int64_t>(N) * (K / G) * E;
   const int64_t nz = ns / 2;
-  repack_qweight_kernel<<<static_cast<unsigned>((nq + T - 1) / T), T, 0, st>>>(q, N, K, E, blobs, stride, off_q);
-  repack_scales_kernel<<<static_cast<unsigned>((ns + T - 1) / T), T, 0, st>>>(s, N, K, G, E, blobs, stride, off_s);
-  repack_zeros_kernel<<<static_cast<unsigned>((nz + T - 1) / T), T, 0, st>>>(z, N, K, G, E, blobs, stride, off_z);
+  repack_qweight_kernel<<<static_cast<unsigned>((nq + T - 1) / T), T, 0, st>>>(q, N, K, gated, E, blobs, stride,
+                                                                                off_q);
+  repack_scales_kernel<<<static_cast<unsigned>((ns + T - 1) / T), T, 0, st>>>(s, N, K, G, gated, E, blobs, stride,
+                                                                               off_s);
+  repack_zeros_kernel<<<static_cast<unsigned>((nz + T - 1) / T), T, 0, st>>>(z, N, K, G, gated, E, blobs, stride,
+                                                                              off_z);
   return launch_status();
 }
 
@@ -136,10 +145,10 @@ int repack_gptq(const int32_t* w13q, const int32_t* w13z, const uint16_t* w13s, 
                 cudaStream_t st) {
   MtpExpertLayout L;
   expert_layout(H, I, G, &L);
-  int r = repack_proj(w13q, w13z, w13s, 2 * I, H, G, E, out, L.bytes, L.w13_qweight, L.w13_scales,
+  int r = repack_proj(w13q, w13z, w13s, 2 * I, H, G, 1, E, out, L.bytes, L.w13_qweight, L.w13_scales,
                       L.w13_zeros, st);
   if (r != MTP_OK) return r;
-  return repack_proj(w2q, w2z, w2s, H, I, G, E, out, L.bytes, L.w2_qweight, L.w2_scales, L.w2_zeros, st);
+  return repack_proj(w2q, w2z, w2s, H, I, G, 0, E, out, L.bytes, L.w2_qweight, L.w2_scales, L.w2_zeros, st);
 }
 
 __global__ void gptq_dequant_kernel(const int32_t* __restrict__ q, const int32_t* __restrict__ z,

@@ -41,7 +41,7 @@ struct FusedArgs {
   float* out_f32;
   int32_t* status;
   int32_t* demand_log;
-  int stages;
+  int stages, sk;             // weight stages in the ring, K per stage
   uint32_t stage_bytes;
   uint32_t xbuf_bytes;
 };

@@ -1,9 +1,9 @@
 // The W4A16 MoE layer forward on sm_100a as one persistent kernel (one CTA
-// per SM, 18 warps). It runs in three phases separated by grid-wide barriers:
+// per SM, 15 warps). It runs in three phases separated by grid-wide barriers:
 //
 //   routing  CTA c routes tokens c, c + G, ... (G = CTAs): router softmax /
-//            top-k / renormalise (warps 0-7, one token each), the shared
-//            expert's sigmoid gate (warps 8-15); each (token, slot) pair is
+//            top-k / renormalise (warps 0-6, one token each) and the shared
+//            expert's sigmoid gate (warps 7-13); each (token, slot) pair is
 //            appended to its expert's list with an atomic counter. Pair order
 //            inside a list does not change any result: every pair is its own
 //            MMA column.
@@ -12,41 +12,51 @@
 //            ascending) from the per-expert counts, and fills the entries of
 //            its own unit ranges into shared memory with the blob address
 //            already resolved through the slot table.
-//   experts  warp-specialised over the work units:
-//          warp 16  weight producer - streams each work unit's packed int4
-//                   strips, fp16 scales and zero nibbles from HBM into a ring
-//                   of shared-memory stages with 1-D bulk copies
-//                   (cp.async.bulk completing on an mbarrier), running ahead
-//                   of the consumers by the ring depth;
-//          warp 17  operand producer - brings the B operand of every token
-//                   block (8 x rows for W1, 8 h rows for W2) into a double
-//                   buffer; before the first W2 unit of a segment it waits
-//                   until all W1 units of that segment have published h;
-//          warps 0-15 consumers - quantise each new block of operand rows
-//                   in shared memory to 16-bit integers (a signed high-byte
-//                   row, an unsigned low-byte row, one scale per row), unpack
-//                   the int4 weights to u8, run exact int32 m16n8k32 MMAs
-//                   (u8 x s8 and u8 x u8) per quantisation group, fold the
-//                   zero point and the scales in fp32, reduce across warps,
-//                   then the epilogue.
+//   experts  warp-specialised pipeline over the work units, with the
+//            5th-generation tensor cores (tcgen05) doing the MMAs:
+//     warp 13  weight producer - streams the int4 weights, fp16 scales and
+//              zero nibbles of each stage (128 rows x SK of K) of each unit
+//              from HBM into a ring of shared-memory stages with 1-D bulk
+//              copies completing on mbarriers;
+//     warp 14  operand producer - brings the 8 bf16 rows of each token block
+//              (x for W1, h for W2) into a double buffer; before the first W2
+//              unit of a segment it waits until every W1 unit of that segment
+//              has published its h columns;
+//     warps 0-7  dequant - quantise each new block of operand rows in place to
+//              16-bit integers laid out as the MMA's B operand (a signed high
+//              byte plane and an unsigned low byte plane, K-major 8x16-byte
+//              core matrices, one scale per row, sums per quantisation group),
+//              and unpack each stage's int4 weights to u8 straight into tensor
+//              memory (the MMA's A operand, lane = weight row);
+//     warp 12  MMA issuer - one thread issues tcgen05.mma kind::i8 (M=128,
+//              N=8, K=32; A u8 from tensor memory, B from shared memory) for
+//              the high and the low byte plane into per-group int32
+//              accumulators in tensor memory, and commits each stage to an
+//              mbarrier;
+//     warps 8-11 epilogue - read the accumulators back (tcgen05.ld), fold
+//              zero point, group scale and row scale in fp32 per group:
+//              acc += s_g * (256 * D_hi + D_lo - z_g * sum_g(x)), then at the
+//              end of a unit write h = silu(gate) * up (W1) or y = acc * w
+//              (W2).
+//   Tensor memory holds a ring of 4 slots, each the u8 A tile of one stage
+//   and the group accumulators of that stage, so dequant, MMA and epilogue of
+//   consecutive stages overlap.
 //
 // Work units, in this order (each CTA takes a contiguous range of each list;
-// a work segment is one token block, so ranges balance and every unit of a
-// segment reuses the same operand rows):
-//   W1 unit (segment, strip pair i): gate rows 16i..16i+15 and up rows
-//      I+16i..I+16i+15 over all of K = H -> h = silu(gate) * up (bf16) for
+// a work segment is one token block, so ranges balance and consecutive units
+// of a segment reuse the same operand rows):
+//   W1 unit (segment, row block b): gate rows 64b..64b+63 and up rows
+//      I+64b..I+64b+63 over all of K = H -> h = silu(gate) * up (bf16) for
 //      every (token, slot) pair of the segment (vLLM fused_moe W1 +
 //      silu_and_mul, tracing/vllm_router_trace.py:19674-19719).
-//   W2 unit (segment, row octet r): down rows 128r..128r+127 over K = I ->
+//   W2 unit (segment, row block b): down rows 128b..128b+127 over K = I ->
 //      y = h . W2^T times the router weight (MUL_ROUTED_WEIGHT, :19761-19782),
 //      fp32 per pair.
 // Then a second grid-wide barrier, after which every CTA combines a slice of
-// the output and clears a slice of the per-call counters: out = sum over the top-k slots in slot order of y +
-// sigmoid(x . w_g) * y_shared (moe_sum :19801 and the shared-expert gate
-// :3994-4031, :4140-4152), so the result is deterministic.
-//
-// Consecutive units of the same single-block segment reuse the operand buffer
-// (the same x or h rows) without a new copy.
+// the output and clears a slice of the per-call counters: out = sum over the
+// top-k slots in slot order of y + sigmoid(x . w_g) * y_shared (moe_sum :19801
+// and the shared-expert gate :3994-4031, :4140-4152), so the result is
+// deterministic.
 //
 // Cross-CTA dependencies go through release/acquire counters. Units never
 // wait on later units and the final barrier is reached by every CTA after
@@ -56,41 +66,78 @@
 // carries on, so it always terminates. A caller-given top-k row that repeats
 // an expert sets value 4 (the repeat is dropped).
 #include "internal.cuh"
-#include "route.cuh"
 
 namespace mtp {
 
-constexpr int kFBM = 8;            // tokens (pairs) per block = MMA N
-constexpr int kCW = 16;            // consumer warps
-constexpr int kCT = kCW * 32;      // consumer threads
-constexpr int kFusedThreads = kCT + 64;
-constexpr int kWProd = kCW;        // weight producer warp
-constexpr int kBProd = kCW + 1;    // operand producer warp
-constexpr int kMaxStages = 4;
-constexpr int kCtrlBytes = 512;
-constexpr int kWsCache = 64;       // work segments cached in shared memory per pass
+constexpr int kFBM = 8;             // pairs per token block = MMA N
+constexpr int kDQ = 8;              // dequant warps 0-7
+constexpr int kEpi0 = 8;            // epilogue warps 8-11
+constexpr int kMmaWarp = 12;
+constexpr int kWProd = 13;          // weight producer warp
+constexpr int kBProd = 14;          // operand producer warp
+constexpr int kWarps = 15;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
+constexpr int kMaxStages = 8;
+constexpr int kTSlots = 4;          // tensor-memory ring slots
+constexpr int kAccs = 4;            // independent accumulators per stage (16 columns each)
+constexpr int kTmemCols = 512;
+constexpr int kCtrlBytes = 1024;
+constexpr int kWsCache = 64;        // work segments cached in shared memory per pass
 constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
-constexpr int kRedBytes = kCW * 2 * 4 * 32 * 4 + 2 * 4 * 32 * 4;
+constexpr int kMaxGroups = 32;      // K / G for K <= 2048, G >= 64
+constexpr int kMaxStageGroups = 4;  // SK / G for SK <= 256, G >= 64
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per layer call
-constexpr int kBarConsumers = 1;   // named barrier id for the consumer warps
-constexpr int kMaxChunks = 32;     // K / 64 for K <= 2048
+constexpr int kBarDequant = 1;      // named barrier: the 8 dequant warps
+constexpr int kBarEpi = 2;          // named barrier: the 4 epilogue warps
+// kind::i8 instruction descriptor: int32 D, A u8, B s8, both K-major, N=16
+// (the 8 high-byte rows then the 8 low-byte rows of a token block), M=128.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 10) | (2u << 17) | (8u << 24);
 
 // ---------------------------------------------------------------------------
 // shared-memory control block and the per-pass work-segment view
 // ---------------------------------------------------------------------------
 struct Ctrl {
-  uint64_t full[kMaxStages];
-  uint64_t empty[kMaxStages];
-  uint64_t xfull[2];
-  uint64_t xempty[2];
+  uint64_t full[kMaxStages];    // weight stage landed (tx count)
+  uint64_t empty[kMaxStages];   // weight stage consumed by the dequant warps
+  uint64_t xfull[2];            // operand rows landed
+  uint64_t xempty[2];           // operand buffer free (MMA commit + 4 epilogue warps)
+  uint64_t qfull[2];            // operand quantised (B operand ready)
+  uint64_t afull[kTSlots];      // A tile of a tensor-memory slot written
+  uint64_t dfull[kTSlots];      // accumulators of a slot complete (MMA commit)
+  uint64_t dempty[kTSlots];     // accumulators of a slot read by the epilogue
+  uint64_t drain;               // final MMA commit
   int stage_valid[kMaxStages];
   int seg_first[2];   // first work segment of the pass range
   int cached[2];      // 1 if the pass range's segments are in the table
   int S;              // work segments of this call
   int gen0;           // grid-barrier generation when the kernel started
+  uint32_t tmem;      // tensor-memory base address
   int scan[32];       // block-scan scratch
 };
 static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
+
+// Per operand buffer: quantisation metadata of its 8 rows.
+struct OperandMeta {
+  float sx[kFBM];                // row scale: x = sx * (256 * hi + lo)
+  float amax[kDQ][kFBM];         // per-warp row maxima (scratch)
+  int xsum[kFBM][kMaxGroups];    // per quantisation group: sum of the 16-bit row values
+};
+
+// Per row and group of one stage, handed from the dequant warps to the
+// epilogue with the tensor-memory slot: scale, zero point, and the sum of the
+// group's int4 values (one partial per K half of the stage).
+struct SlotScales {
+  float s[kMaxStageGroups][128];
+  uint16_t q[2][kMaxStageGroups][128];
+  uint8_t z[kMaxStageGroups][128];
+};
+
+// Units per work segment: W1 row blocks of 64 gate + 64 up rows, W2 row blocks
+// of 128 rows.
+__device__ __forceinline__ int units_per_segment(const FusedArgs& a, int pass) {
+  return pass == 0 ? a.I / 64 : a.H / 128;
+}
 
 struct Pass {
   int ub, ue, per;    // unit range and units per segment
@@ -120,12 +167,13 @@ __device__ __forceinline__ void unit_range(int total_units, int& b, int& e) {
 __device__ __forceinline__ Pass make_pass(const FusedArgs& a, const Ctrl& cb, const int* table, int pass) {
   Pass P;
   const int S = cb.S;
-  P.per = pass == 0 ? a.I / 16 : a.H / 128;
+  P.per = units_per_segment(a, pass);
   unit_range(S * P.per, P.ub, P.ue);
   P.seg_first = cb.seg_first[pass];
   P.table = cb.cached[pass] ? table + pass * kWsCache * kWsInts : a.wseg + static_cast<size_t>(P.seg_first) * kWsInts;
   return P;
 }
+
 
 // A unit reuses the operand buffer of the previous unit when both belong to
 // the same single-block segment (same rows).
@@ -153,6 +201,7 @@ __device__ __forceinline__ bool grid_sync(const FusedArgs& a, int target, uint64
   }
   while (static_cast<int>(static_cast<uint32_t>(ld_acquire_gpu(a.bar + 1)) - static_cast<uint32_t>(target)) < 0) {
     if (global_timer_ns() > deadline) return false;
+    __nanosleep(32);
   }
   return true;
 }
@@ -260,22 +309,24 @@ __device__ __forceinline__ void router_warp(const float* __restrict__ row, int E
   *id_out = my_id;
 }
 
-// Phase 1 (consumer warps): route this CTA's tokens, count and list the
-// (token, slot) pairs per expert, and compute the shared-expert gate. Warps
-// 0-7 route a token each; warps 8-15 compute the gates of the same tokens.
-// `scratch` holds 8 x E floats (the stage ring, still unused).
-__device__ void route_phase(const FusedArgs& a, int ctid, float* scratch) {
-  const int warp = ctid >> 5, lane = ctid & 31;
+// Phase 1: route this CTA's tokens, count and list the (token, slot) pairs per
+// expert, and compute the shared-expert gate. Warps 0-6 route a token each;
+// warps 7-13 compute the gates of the same tokens. `scratch` holds 7 x E
+// floats (the stage ring, still unused).
+__device__ void route_phase(const FusedArgs& a, float* scratch) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2 * kRouteWarps) return;
   const int G = gridDim.x;
-  for (int i0 = 0; static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * i0 < a.M; i0 += 8) {
-    const int64_t t64 = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * (i0 + (warp & 7));
+  const int slot = warp % kRouteWarps;
+  for (int i0 = 0; static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * i0 < a.M; i0 += kRouteWarps) {
+    const int64_t t64 = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(G) * (i0 + slot);
     if (t64 >= a.M) continue;
     const int t = static_cast<int>(t64);
-    if (warp < 8) {
+    if (warp < kRouteWarps) {
       int id = -1;
       if (a.logits) {
         float w;
-        router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + warp * a.E, &w, &id);
+        router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + slot * a.E, &w, &id);
         if (lane < a.k) {
           a.topk_w[t * a.k + lane] = w;
           a.topk_ids[t * a.k + lane] = id;
@@ -367,42 +418,48 @@ __device__ void fill_entry(const FusedArgs& a, int s, int shared_ws, const int* 
 // Phase 2 (all threads, after the grid barrier): every CTA derives the work
 // segments from the per-expert counts and fills the table entries of its own
 // two unit ranges; CTA 0 also writes the demand log and the miss counts.
-// `scratch` holds 2E + 1 ints (the operand buffers, still unused).
+// `scratch` holds 2E + 1 ints (the stage ring, still unused).
 __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scratch) {
   const int tid = threadIdx.x, nt = blockDim.x;
   int* cnt = scratch;           // [E]
   int* sbase = scratch + a.E;   // [E + 1]
-  // each thread owns experts [2 tid, 2 tid + 2) (E <= 1024 < 2 * 576)
-  int c0 = 0, c1 = 0;
-  if (2 * tid < a.E) c0 = min(__ldcg(a.cnt + 2 * tid), a.M);
-  if (2 * tid + 1 < a.E) c1 = min(__ldcg(a.cnt + 2 * tid + 1), a.M);
-  const int n0 = (c0 + kFBM - 1) / kFBM, n1 = (c1 + kFBM - 1) / kFBM;
-  int total;
-  const int ex = cta_exclusive_scan(n0 + n1, &total, cb.scan);
-  if (2 * tid < a.E) {
-    cnt[2 * tid] = c0;
-    sbase[2 * tid] = ex;
+  // thread tid owns experts [tid * per, tid * per + per)
+  const int per = (a.E + nt - 1) / nt;  // <= 3 for E <= 1024
+  const int e0 = tid * per;
+  int c[3] = {0, 0, 0};
+  int nseg = 0, nused = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    if (j < per && e0 + j < a.E) {
+      c[j] = min(__ldcg(a.cnt + e0 + j), a.M);
+      nseg += (c[j] + kFBM - 1) / kFBM;
+      nused += c[j] > 0;
+    }
   }
-  if (2 * tid + 1 < a.E) {
-    cnt[2 * tid + 1] = c1;
-    sbase[2 * tid + 1] = ex + n0;
+  int total;
+  int ex = cta_exclusive_scan(nseg, &total, cb.scan);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    if (j < per && e0 + j < a.E) {
+      cnt[e0 + j] = c[j];
+      sbase[e0 + j] = ex;
+      ex += (c[j] + kFBM - 1) / kFBM;
+    }
   }
   if (tid == 0) sbase[a.E] = total;
   const int shared_ws = a.has_shared ? (a.M + kFBM - 1) / kFBM : 0;
   const int S = shared_ws + total;
   if (tid == 0) cb.S = S;
   if (blockIdx.x == 0) {
-    const int u0 = c0 > 0, u1 = c1 > 0;
-    int nused;
-    const int rank = cta_exclusive_scan(u0 + u1, &nused, cb.scan);
-    if (a.demand_log) {
-      if (tid == 0) a.demand_log[0] = nused;
-      if (u0) a.demand_log[1 + rank] = 2 * tid;
-      if (u1) a.demand_log[1 + rank + u0] = 2 * tid + 1;
-    }
-    for (int j = 0; j < 2; ++j) {
-      const int e = 2 * tid + j;
-      if (e < a.E && (j == 0 ? u0 : u1)) {
+    int nall;
+    int rank = cta_exclusive_scan(nused, &nall, cb.scan);
+    if (a.demand_log && tid == 0) a.demand_log[0] = nall;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int e = e0 + j;
+      if (j < per && e < a.E && c[j] > 0) {
+        if (a.demand_log) a.demand_log[1 + rank] = e;
+        ++rank;
         const int slot = a.slot_table ? a.slot_table[e] : e;
         if (slot < 0) atomicAdd(a.host_blobs ? a.status + 0 : a.status + 1, 1);
       }
@@ -410,11 +467,11 @@ __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scrat
   }
   __syncthreads();
   for (int pass = 0; pass < 2; ++pass) {
-    const int per = pass == 0 ? a.I / 16 : a.H / 128;
+    const int upg = units_per_segment(a, pass);
     int ub, ue;
-    unit_range(S * per, ub, ue);
-    const int first = ub / per;
-    const int last = ue > ub ? (ue - 1) / per : first - 1;
+    unit_range(S * upg, ub, ue);
+    const int first = ub / upg;
+    const int last = ue > ub ? (ue - 1) / upg : first - 1;
     const int n = last - first + 1;
     const bool cached = n <= kWsCache;
     if (tid == 0) {
@@ -441,44 +498,30 @@ __device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
   return v;
 }
 
-// Byte ranges of a unit inside the expert blob and inside the stage.
+// ---------------------------------------------------------------------------
+// producers
+// ---------------------------------------------------------------------------
+// Stage s of unit (pass, row block b): K range [s * SK, (s + 1) * SK) of the
+// block, three contiguous byte ranges of the blob.
 struct Piece {
   uint32_t src_off;
   uint32_t dst_off;
   uint32_t bytes;
 };
 
-__device__ __forceinline__ int w1_pieces(const FusedArgs& a, int strip, Piece* p) {
-  const uint32_t sb = 8u * a.H;  // one 16-row strip over K = H
-  const uint32_t scb = static_cast<uint32_t>(a.H / a.G) * 32u;
-  const uint32_t zpb = static_cast<uint32_t>(a.H / a.G) * 8u;
-  const uint32_t up = a.I / 16 + strip;
-  const uint32_t L13 = static_cast<uint32_t>(a.L.w13_qweight), S13 = static_cast<uint32_t>(a.L.w13_scales),
-                 Z13 = static_cast<uint32_t>(a.L.w13_zeros);
-  p[0] = {L13 + strip * sb, 0, sb};
-  p[1] = {L13 + up * sb, sb, sb};
-  p[2] = {S13 + strip * scb, 2 * sb, scb};
-  p[3] = {S13 + up * scb, 2 * sb + scb, scb};
-  p[4] = {Z13 + strip * zpb, 2 * sb + 2 * scb, zpb};
-  p[5] = {Z13 + up * zpb, 2 * sb + 2 * scb + zpb, zpb};
-  return 6;
+__device__ __forceinline__ void stage_pieces(const FusedArgs& a, int pass, int b, int s, Piece* p) {
+  const int K = pass == 0 ? a.H : a.I;
+  const uint32_t q0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_qweight : a.L.w2_qweight);
+  const uint32_t s0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_scales : a.L.w2_scales);
+  const uint32_t z0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_zeros : a.L.w2_zeros);
+  const uint32_t chunk = static_cast<uint32_t>(b) * (K / 32) + static_cast<uint32_t>(s) * (a.sk / 32);
+  const uint32_t grp = static_cast<uint32_t>(b) * (K / a.G) + static_cast<uint32_t>(s) * (a.sk / a.G);
+  const uint32_t wb = static_cast<uint32_t>(a.sk) * 64u, sb = (a.sk / a.G) * 256u, zb = (a.sk / a.G) * 64u;
+  p[0] = {q0 + chunk * 2048u, 0u, wb};
+  p[1] = {s0 + grp * 256u, wb, sb};
+  p[2] = {z0 + grp * 64u, wb + sb, zb};
 }
 
-__device__ __forceinline__ int w2_pieces(const FusedArgs& a, int octet, Piece* p) {
-  const uint32_t ob = 64u * a.I;  // 8 strips of 16 rows over K = I
-  const uint32_t scb = 8u * static_cast<uint32_t>(a.I / a.G) * 32u;
-  const uint32_t zpb = 8u * static_cast<uint32_t>(a.I / a.G) * 8u;
-  const uint32_t L2 = static_cast<uint32_t>(a.L.w2_qweight), S2 = static_cast<uint32_t>(a.L.w2_scales),
-                 Z2 = static_cast<uint32_t>(a.L.w2_zeros);
-  p[0] = {L2 + octet * ob, 0, ob};
-  p[1] = {S2 + octet * scb, ob, scb};
-  p[2] = {Z2 + octet * zpb, ob + scb, zpb};
-  return 3;
-}
-
-// ---------------------------------------------------------------------------
-// producers
-// ---------------------------------------------------------------------------
 __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages,
                                 uint64_t deadline) {
   const int lane = threadIdx.x & 31;
@@ -486,52 +529,53 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
   uint32_t ph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
+    const int nst = (pass == 0 ? a.H : a.I) / a.sk;
     for (int u = P.ub; u < P.ue; ++u) {
-      const int seg = u / P.per, idx = u % P.per;
+      const int seg = u / P.per, b = u % P.per;
       const int* e = ws_entry(P, seg);
       const uint8_t* blob = ws_blob(e);
       const bool host = (e[3] & 2) != 0;
-      Piece pc[6];
-      const int n = pass == 0 ? w1_pieces(a, idx, pc) : w2_pieces(a, idx, pc);
-      if (!mbar_wait(smem_u32(&cb.empty[st]), ph ^ 1u, deadline) && lane == 0) record_timeout(a);
-      uint8_t* dst = stages + static_cast<size_t>(st) * a.stage_bytes;
-      const uint32_t full = smem_u32(&cb.full[st]);
-      if (lane == 0) cb.stage_valid[st] = blob != nullptr;
-      if (blob != nullptr && !host) {
-        if (lane == 0) {
-          uint32_t total = 0;
-          for (int i = 0; i < n; ++i) total += pc[i].bytes;
-          mbar_arrive_expect_tx(full, total);
-          for (int i = 0; i < n; ++i) bulk_g2s(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full);
-        }
-      } else {
-        // Pinned host memory (demand fetch over the host link): a warp copy
-        // with eight 16-byte loads in flight per lane.
-        if (blob != nullptr) {
-          for (int i = 0; i < n; ++i) {
-            const uint8_t* src = blob + pc[i].src_off;
-            uint8_t* d = dst + pc[i].dst_off;
-            for (uint32_t o = lane * 16u; o < pc[i].bytes; o += 32u * 16u * 8u) {
-              uint4 v[8];
+      for (int s = 0; s < nst; ++s) {
+        Piece pc[3];
+        stage_pieces(a, pass, b, s, pc);
+        if (!mbar_wait(smem_u32(&cb.empty[st]), ph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        uint8_t* dst = stages + static_cast<size_t>(st) * a.stage_bytes;
+        const uint32_t full = smem_u32(&cb.full[st]);
+        if (lane == 0) cb.stage_valid[st] = blob != nullptr;
+        if (blob != nullptr && !host) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(full, pc[0].bytes + pc[1].bytes + pc[2].bytes);
+            for (int i = 0; i < 3; ++i) bulk_g2s(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full);
+          }
+        } else {
+          // Pinned host memory (demand fetch over the host link): a warp copy
+          // with eight 16-byte loads in flight per lane.
+          if (blob != nullptr) {
+            for (int i = 0; i < 3; ++i) {
+              const uint8_t* src = blob + pc[i].src_off;
+              uint8_t* d = dst + pc[i].dst_off;
+              for (uint32_t o = lane * 16u; o < pc[i].bytes; o += 32u * 16u * 8u) {
+                uint4 v[8];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const uint32_t oo = o + j * 512u;
-                if (oo < pc[i].bytes) v[j] = ldg_stream16(src + oo);
-              }
+                for (int j = 0; j < 8; ++j) {
+                  const uint32_t oo = o + j * 512u;
+                  if (oo < pc[i].bytes) v[j] = ldg_stream16(src + oo);
+                }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const uint32_t oo = o + j * 512u;
-                if (oo < pc[i].bytes) *reinterpret_cast<uint4*>(d + oo) = v[j];
+                for (int j = 0; j < 8; ++j) {
+                  const uint32_t oo = o + j * 512u;
+                  if (oo < pc[i].bytes) *reinterpret_cast<uint4*>(d + oo) = v[j];
+                }
               }
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(full);
-      }
-      if (++st == a.stages) {
-        st = 0;
-        ph ^= 1u;
+        if (++st == a.stages) {
+          st = 0;
+          ph ^= 1u;
+        }
       }
     }
   }
@@ -551,16 +595,17 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
       const int seg = u / P.per;
       if (reuses_operand(P, u)) continue;
       const int* e = ws_entry(P, seg);
-      const int nb = e[2];
       if (pass == 1 && seg != waited_seg) {
         // every W1 unit of this segment has published its h columns
         if (lane == 0) {
           bool ok = true;
-          while (ld_acquire_gpu(a.seg_done + seg) < a.I / 16) {
+          const int need = units_per_segment(a, 0);
+          while (ld_acquire_gpu(a.seg_done + seg) < need) {
             if (global_timer_ns() > deadline) {
               ok = false;
               break;
             }
+            __nanosleep(64);
           }
           if (!ok) record_timeout(a);
           fence_proxy_async_global();
@@ -568,19 +613,183 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
         __syncwarp();
         waited_seg = seg;
       }
-      for (int blk = 0; blk < nb; ++blk) {
-        if (!mbar_wait(smem_u32(&cb.xempty[xb]), xph ^ 1u, deadline) && lane == 0) record_timeout(a);
-        const int p = lane < kFBM ? e[4 + blk * kFBM + lane] : -1;
-        const unsigned valid = __ballot_sync(kFullMask, p >= 0);
-        const uint32_t xfull = smem_u32(&cb.xfull[xb]);
-        if (lane == 0) mbar_arrive_expect_tx(xfull, __popc(valid) * row_bytes);
-        __syncwarp();
-        if (p >= 0) {
-          const uint8_t* src = pass == 0
-                                   ? reinterpret_cast<const uint8_t*>(a.x + static_cast<int64_t>(pair_token(a, p)) * a.H)
-                                   : reinterpret_cast<const uint8_t*>(a.hbuf + static_cast<int64_t>(p) * a.I);
-          bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
+      if (!mbar_wait(smem_u32(&cb.xempty[xb]), xph ^ 1u, deadline) && lane == 0) record_timeout(a);
+      const int p = lane < kFBM ? e[4 + lane] : -1;
+      const unsigned valid = __ballot_sync(kFullMask, p >= 0);
+      const uint32_t xfull = smem_u32(&cb.xfull[xb]);
+      if (lane == 0) mbar_arrive_expect_tx(xfull, __popc(valid) * row_bytes);
+      __syncwarp();
+      if (p >= 0) {
+        const uint8_t* src = pass == 0
+                                 ? reinterpret_cast<const uint8_t*>(a.x + static_cast<int64_t>(pair_token(a, p)) * a.H)
+                                 : reinterpret_cast<const uint8_t*>(a.hbuf + static_cast<int64_t>(p) * a.I);
+        bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
+      }
+      if (++xb == 2) {
+        xb = 0;
+        xph ^= 1u;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dequant warps (0-7): operand quantisation and the A tiles in tensor memory
+// ---------------------------------------------------------------------------
+// Quantise the 8 bf16 rows of an operand buffer in place into 16-bit integers
+// v = 256 * hi + lo' + 128 laid out as the MMA's B operand: the signed high
+// bytes hi at [0, 8K), the signed offset low bytes lo' = (v & 255) - 128 at
+// [8K, 16K), each plane K-major in 8-row x 16-byte core matrices ((n, k) at
+// (k / 16) * 128 + n * 16 + k % 16), so one N=16 MMA covers both planes; one
+// scale per row and per-group sums of v. Thread (warp w, lane = 4n + q)
+// owns the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i, so every
+// plane store of a warp is one contiguous 128-byte core matrix. All values
+// are read before the first barrier and written after it (the output
+// overlaps the input).
+template <int G>
+__device__ __forceinline__ void quantize_rows(uint8_t* rows, OperandMeta& meta, int K) {
+  const int t = threadIdx.x, w = t >> 5, lane = t & 31, n = lane >> 2, q = lane & 3;
+  const int iters = K / 128;  // <= 16
+  const uint8_t* row = rows + n * (2 * K + 16);
+  uint2 raw[16];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    raw[i] = make_uint2(0u, 0u);
+    if (i < iters) {
+      raw[i] = *reinterpret_cast<const uint2*>(row + 2 * (16 * (w + 8 * i) + 4 * q));
+      const uint32_t m0 = __vmaxu2(raw[i].x & 0x7fff7fffu, raw[i].y & 0x7fff7fffu);
+      mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
+    }
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 2));
+  if (q == 0) meta.amax[w][n] = mx;
+  for (int i = t; i < kFBM * kMaxGroups; i += kDQ * 32) (&meta.xsum[0][0])[i] = 0;
+  named_bar_sync(kBarDequant, kDQ * 32);
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kDQ; ++j) amax = fmaxf(amax, meta.amax[j][n]);
+  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+  uint8_t* hi_plane = rows;
+  uint8_t* lo_plane = rows + 8 * K;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i < iters) {  // warp-uniform
+      const int cc = w + 8 * i;
+      uint32_t hw = 0u, lw = 0u;
+      int sum = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t h = (b < 2 ? raw[i].x : raw[i].y) >> (16 * (b & 1));
+        const int v = max(-32767, min(32767, __float2int_rn(__uint_as_float(h << 16) * inv)));
+        sum += v;
+        hw |= (static_cast<uint32_t>(v >> 8) & 0xffu) << (8 * b);
+        lw |= ((static_cast<uint32_t>(v) & 0xffu) ^ 0x80u) << (8 * b);
+      }
+      const int off = cc * 128 + n * 16 + 4 * q;
+      *reinterpret_cast<uint32_t*>(hi_plane + off) = hw;
+      *reinterpret_cast<uint32_t*>(lo_plane + off) = lw;
+      sum += __shfl_xor_sync(kFullMask, sum, 1);
+      sum += __shfl_xor_sync(kFullMask, sum, 2);
+      if (q == 0) atomicAdd(&meta.xsum[n][(16 * cc) / G], sum);
+    }
+  }
+  if (t < kFBM) {
+    float m = 0.f;
+    for (int j = 0; j < kDQ; ++j) m = fmaxf(m, meta.amax[j][t]);
+    meta.sx[t] = m / 32767.f;
+  }
+  fence_proxy_async_shared();  // the plane stores are read by the tensor cores
+  named_bar_sync(kBarDequant, kDQ * 32);
+}
+
+template <int SK, int G>
+__device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages, uint8_t* xbufs,
+                              OperandMeta* metas, SlotScales* scales, uint64_t deadline) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int r = 32 * quad + lane;  // weight row = tensor-memory lane
+  const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
+  constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
+  constexpr uint32_t acols = SK / 4;
+  int st = 0, ts = 0, xb = 0;
+  uint32_t ph = 0, tph = 0, xph = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const Pass P = make_pass(a, cb, table, pass);
+    const int K = pass == 0 ? a.H : a.I;
+    const int nst = K / SK;
+    for (int u = P.ub; u < P.ue; ++u) {
+      const bool reuse = reuses_operand(P, u);
+      const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
+      if (!reuse) {
+        if (!mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && threadIdx.x == 0) record_timeout(a);
+        quantize_rows<G>(xbufs + xb * a.xbuf_bytes, metas[xb], K);
+        if (threadIdx.x == 0) mbar_arrive(smem_u32(&cb.qfull[xb]));
+      }
+      for (int s = 0; s < nst; ++s) {
+        if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && lane == 0) record_timeout(a);
+        if (!mbar_wait(smem_u32(&cb.dempty[ts]), tph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        const bool valid = cb.stage_valid[st] != 0;
+        const uint8_t* stage = stages + static_cast<size_t>(st) * a.stage_bytes;
+        const uint32_t sbase = smem_u32(stage);
+        const uint32_t tcol = cb.tmem + lane_addr + ts * acols;
+        SlotScales& ss = scales[ts];
+#pragma unroll
+        for (int g = 0; g < gps; ++g) ss.q[half][g][r] = 0;
+#pragma unroll
+        for (int cp = 0; cp < my_chunks; cp += 2) {
+          const int c0 = half * my_chunks + cp;
+          uint32_t v[16];
+          uint32_t qsum = 0;  // sum of the 64 int4 values of the two chunks
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) wv = lds128(sbase + ((c0 + cc) * 128 + r) * 16);
+            const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t lo = w4[j] & 0x0F0F0F0Fu, hi = (w4[j] >> 4) & 0x0F0F0F0Fu;
+              v[cc * 8 + 2 * j] = lo;
+              v[cc * 8 + 2 * j + 1] = hi;
+              qsum += ((lo + hi) * 0x01010101u) >> 24;  // byte sums <= 30: no carry
+            }
+          }
+          tmem_st16(tcol + c0 * 8, v);
+          ss.q[half][(c0 * 32) / G][r] += static_cast<uint16_t>(qsum);
         }
+        if (half == 0) {
+          const uint16_t* sc = reinterpret_cast<const uint16_t*>(stage + SK * 64);
+          const uint8_t* zp = stage + SK * 64 + gps * 256;
+#pragma unroll
+          for (int g = 0; g < gps; ++g) {
+            float s_ = 0.f;
+            uint32_t z_ = 8;
+            if (valid) {
+              s_ = __half2float(__ushort_as_half(sc[g * 128 + r]));
+              if (a.zero_mode == MTP_ZERO_RAW) z_ = (zp[g * 64 + (r >> 1)] >> (4 * (r & 1))) & 0xF;
+            }
+            ss.s[g][r] = s_;
+            ss.z[g][r] = static_cast<uint8_t>(z_);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&cb.afull[ts]));
+          mbar_arrive(smem_u32(&cb.empty[st]));
+        }
+        if (++st == a.stages) {
+          st = 0;
+          ph ^= 1u;
+        }
+        if (++ts == kTSlots) {
+          ts = 0;
+          tph ^= 1u;
+        }
+      }
+      if (!keep) {
         if (++xb == 2) {
           xb = 0;
           xph ^= 1u;
@@ -591,335 +800,256 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
 }
 
 // ---------------------------------------------------------------------------
-// consumers
+// MMA issuer (warp 12, one thread)
 // ---------------------------------------------------------------------------
-// Per operand buffer: quantisation metadata of its 8 rows.
-struct OperandMeta {
-  float sx[kFBM];              // row scale: x = sx * (256 * hi + lo)
-  float amax[kFBM][2];         // per-half row maxima (scratch)
-  int xsum[kFBM][kMaxChunks];  // per 64-wide chunk: sum of the 16-bit row values
-};
-
-__device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
-  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-// Quantise the 8 bf16 rows of an operand buffer in place into 16-bit
-// integers split into a signed high byte row and an unsigned low byte row
-// (row n: hi at [0, K), lo at [K, 2K) of its 2K + 16 byte slot), with a
-// per-row scale and per-64-element-chunk sums. 512 consumer threads, 64 per
-// row; thread tr owns the 4-element groups j = tr + 64 i, so every shared-
-// memory access of a warp is contiguous. All values are read before the first
-// barrier and written after it (the output overlaps the input).
-__device__ __forceinline__ void quantize_rows(uint8_t* rows, OperandMeta& meta, int K, int ctid) {
-  const int n = ctid >> 6, tr = ctid & 63;
-  const int ng = K / 4;  // 16..512 groups per row
-  uint8_t* row = rows + n * (2u * K + 16u);
-  uint2 raw[8];  // bf16 pairs, kept packed until the scale is known
-  float mx = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = tr + 64 * i;
-    raw[i] = make_uint2(0u, 0u);
-    if (j < ng) {
-      raw[i] = *reinterpret_cast<const uint2*>(row + 8 * j);
-      const uint32_t m0 = __vmaxu2(raw[i].x & 0x7fff7fffu, raw[i].y & 0x7fff7fffu);
-      mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
-    }
-  }
-  mx = warp_max(mx);
-  if ((ctid & 31) == 0) meta.amax[n][(ctid >> 5) & 1] = mx;
-  named_bar_sync(kBarConsumers, kCT);
-  const float amax = fmaxf(meta.amax[n][0], meta.amax[n][1]);
-  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (64 * i < ng) {  // warp-uniform: ng is a multiple of 16, the shuffles stay converged
-      const int j = tr + 64 * i;
-      int sum = 0;
-      if (j < ng) {
-        uint32_t hw = 0u, lw = 0u;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t h = (b < 2 ? raw[i].x : raw[i].y) >> (16 * (b & 1));
-          const int q = max(-32767, min(32767, __float2int_rn(__uint_as_float(h << 16) * inv)));
-          sum += q;
-          hw |= (static_cast<uint32_t>(q >> 8) & 0xffu) << (8 * b);
-          lw |= (static_cast<uint32_t>(q) & 0xffu) << (8 * b);
-        }
-        *reinterpret_cast<uint32_t*>(row + 4 * j) = hw;
-        *reinterpret_cast<uint32_t*>(row + K + 4 * j) = lw;
-      }
-      // a 64-element chunk is the 16 groups of 16 consecutive lanes
-      sum += __shfl_xor_sync(kFullMask, sum, 1);
-      sum += __shfl_xor_sync(kFullMask, sum, 2);
-      sum += __shfl_xor_sync(kFullMask, sum, 4);
-      sum += __shfl_xor_sync(kFullMask, sum, 8);
-      if ((tr & 15) == 0 && j < ng) meta.xsum[n][j >> 4] = sum;
-    }
-  }
-  if (tr == 0) meta.sx[n] = amax / 32767.f;
-  named_bar_sync(kBarConsumers, kCT);
-}
-
-// B operands (high and low byte rows) of one k32 step for this lane's
-// ldmatrix row: matrices hi[k0..], hi[k0+16..], lo[k0..], lo[k0+16..].
-__device__ __forceinline__ void load_b(uint32_t xbase, uint32_t rs, int K, int row, int mat, int k0,
-                                       uint32_t (&b)[4]) {
-  const uint32_t addr = xbase + row * rs + (mat >= 2 ? K : 0) + k0 + 16 * (mat & 1);
-  ldsm_x4(addr, b[0], b[1], b[2], b[3]);
-}
-
-__device__ __forceinline__ void zero_rows_of(uint32_t zb, int zero_mode, int& z0, int& z1) {
-  if (zero_mode == MTP_ZERO_SYM8) {
-    z0 = z1 = 8;
-  } else {
-    z0 = zb & 0xF;
-    z1 = zb >> 4;
-  }
-}
-
-// acc += s_row * (256 * hi + lo - z_row * xsum_col) for the 4 accumulator
-// elements of this lane (rows g, g+8; columns 2t, 2t+1).
-__device__ __forceinline__ void fold_int(float (&acc)[4], const int (&dh)[4], const int (&dl)[4], uint32_t scw,
-                                         int z0, int z1, int xs0, int xs1) {
-  const float2 s = half2_bits_to_float2(scw);
-  acc[0] = fmaf(static_cast<float>(256 * dh[0] + dl[0] - z0 * xs0), s.x, acc[0]);
-  acc[1] = fmaf(static_cast<float>(256 * dh[1] + dl[1] - z0 * xs1), s.x, acc[1]);
-  acc[2] = fmaf(static_cast<float>(256 * dh[2] + dl[2] - z1 * xs0), s.y, acc[2]);
-  acc[3] = fmaf(static_cast<float>(256 * dh[3] + dl[3] - z1 * xs1), s.y, acc[3]);
-}
-
-template <int W1C, int W2C>
-__device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages, uint8_t* xbufs,
-                          OperandMeta* metas, float* red, uint64_t deadline) {
-  const int ctid = threadIdx.x;  // 0..511
-  const int warp = ctid >> 5, lane = ctid & 31, g = lane >> 2, t = lane & 3;
-  const int nkw = a.H / 64 / W1C;  // warps along K in W1 (<= 16)
-  const int cpg = a.G / 64;        // 64-wide chunks per quantisation group
-  int st = 0, xb = 0;
-  uint32_t ph = 0, xph = 0;
-  const int ld_row = lane & 7, ld_mat = lane >> 3;  // ldmatrix row address of this lane
-  int published = 0;  // W1 units of the current segment not yet published
-
+template <int SK, int G>
+__device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs, uint64_t deadline) {
+  constexpr int chunks = SK / 32;
+  constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
+  constexpr int cpg = G / 32, subs = kAccs / (SK / G);
+  int ts = 0, xb = 0;
+  uint32_t tph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int K = pass == 0 ? a.H : a.I;
-    const uint32_t rs = 2u * K + 16u;
+    const int nst = K / SK;
     for (int u = P.ub; u < P.ue; ++u) {
-      const int seg = u / P.per, idx = u % P.per;
-      const int* e = ws_entry(P, seg);
-      const int nb = e[2];
       const bool reuse = reuses_operand(P, u);
       const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
-      if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && ctid == 0) record_timeout(a);
-      const bool wvalid = cb.stage_valid[st] != 0;
-      const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
-      for (int blk = 0; blk < nb; ++blk) {
-        OperandMeta& meta = metas[xb];
-        uint8_t* xrows = xbufs + xb * a.xbuf_bytes;
-        if (!reuse) {
-          if (!mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && ctid == 0) record_timeout(a);
-          quantize_rows(xrows, meta, K, ctid);
+      if (!reuse && !mbar_wait(smem_u32(&cb.qfull[xb]), xph, deadline)) record_timeout(a);
+      const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
+      for (int s = 0; s < nst; ++s) {
+        if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline)) record_timeout(a);
+        tc_fence_after();
+        const uint32_t a_t = cb.tmem + ts * acols;
+        const uint32_t d_t = cb.tmem + kTSlots * acols + ts * dcols;
+        // B: 16 rows = the high plane's 8 rows, then (SBO = 8K bytes on) the low
+        // plane's; chunk c of 32 k starts 256 bytes further (start field +16).
+        // Four independent accumulators per stage, issued round robin, so one
+        // MMA's latency hides behind the next three: accumulator d holds the
+        // chunks c of group d / subs with c % cpg = d % subs (mod subs).
+        const uint64_t desc0 = smem_desc_kmajor(xbase + s * chunks * 256, 128, 8 * K);
+#pragma unroll
+        for (int t = 0; t < cpg / subs; ++t) {
+#pragma unroll
+          for (int d = 0; d < kAccs; ++d) {
+            const int c = (d / subs) * cpg + t * subs + (d % subs);
+            umma_i8_ts(d_t + d * 16, a_t + c * 8, desc0 + 16 * c, kIdesc, t != 0);
+          }
         }
-        const uint32_t xbase = smem_u32(xrows);
-        const int* cols = e + 4 + blk * kFBM;
-        if (pass == 0) {
-          // ------------------------------ W1 ------------------------------
-          float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-          if (wvalid && warp < nkw) {
-            const uint32_t sb = 8u * a.H, scb = (a.H / a.G) * 32u, zpb = (a.H / a.G) * 8u;
-            int dh[2][4], dl[2][4];
-            int xs0 = 0, xs1 = 0;
-#pragma unroll
-            for (int j = 0; j < W1C; ++j) {
-              const int c = warp * W1C + j;
-              uint4 w[2];
-              w[0] = lds128(sbase + (c * 32 + lane) * 16);
-              w[1] = lds128(sbase + sb + (c * 32 + lane) * 16);
-#pragma unroll
-              for (int s2 = 0; s2 < 2; ++s2) {
-                uint32_t b[4];
-                load_b(xbase, rs, K, ld_row, ld_mat, 64 * c + 32 * s2, b);
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  uint32_t A[4];
-                  unpack_u8(pick(w[q], 2 * s2), pick(w[q], 2 * s2 + 1), A);
-                  if (s2 == 0 && (j == 0 || c % cpg == 0)) {
-                    imma_u8s8_zc(dh[q], A, b[0], b[1]);
-                    imma_u8u8_zc(dl[q], A, b[2], b[3]);
-                  } else {
-                    imma_u8s8(dh[q], A, b[0], b[1]);
-                    imma_u8u8(dl[q], A, b[2], b[3]);
-                  }
-                }
-              }
-              xs0 += meta.xsum[2 * t][c];
-              xs1 += meta.xsum[2 * t + 1][c];
-              if ((c + 1) % cpg == 0 || j == W1C - 1) {
-                const int grp = c / cpg;
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  const uint32_t scw = lds32(sbase + 2 * sb + q * scb + (grp * 8 + g) * 4);
-                  const uint32_t zb =
-                      a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 2 * sb + 2 * scb + q * zpb + grp * 8 + g) : 0x88u;
-                  int z0, z1;
-                  zero_rows_of(zb, a.zero_mode, z0, z1);
-                  fold_int(acc[q], dh[q], dl[q], scw, z0, z1, xs0, xs1);
-                }
-                xs0 = xs1 = 0;
-              }
-            }
-          }
-          if (!keep) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&cb.xempty[xb]));
-          }
-          if (warp < nkw) {
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int r = 0; r < 4; ++r) red[((warp * 2 + q) * 4 + r) * 32 + lane] = acc[q][r];
-          }
-          named_bar_sync(kBarConsumers, kCT);
-          {
-            // thread 4m+s: position m = (r, l) of the 16x8 tile, s = (strip,
-            // half of the K warps); halves summed, then gate/up met by shuffle
-            const int m = ctid >> 2, sub = ctid & 3, q = sub >> 1, half = sub & 1;
-            float v = 0.f;
-            for (int w = half; w < nkw; w += 2) v += red[w * 256 + q * 128 + m];
-            v += __shfl_xor_sync(kFullMask, v, 1);
-            const float up = __shfl_xor_sync(kFullMask, v, 2);
-            if (sub == 0) {
-              const int r = m >> 5, l = m & 31;
-              const int col = 2 * (l & 3) + (r & 1);
-              const int p = cols[col];
-              if (p >= 0) {
-                const int row = (l >> 2) + 8 * (r >> 1);
-                const float sx = meta.sx[col];
-                a.hbuf[static_cast<int64_t>(p) * a.I + 16 * idx + row] =
-                    __bfloat16_as_ushort(__float2bfloat16(silu(v * sx) * (up * sx)));
-              }
-            }
-          }
-          // protects red from the next unit and orders the h stores before the
-          // release below
-          named_bar_sync(kBarConsumers, kCT);
-          // publish this CTA's h columns of the segment once, when it leaves
-          // the segment (or its range)
-          ++published;
-          if (blk == nb - 1 && (u + 1 == P.ue || (u + 1) / P.per != seg)) {
-            if (ctid == 0) red_release_gpu_add(a.seg_done + seg, published);
-            published = 0;
-          }
-        } else {
-          // ------------------------------ W2 ------------------------------
-          const int sidx = warp >> 1, hk = warp & 1;
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
-          if (wvalid) {
-            const uint32_t sb = 8u * a.I;  // one strip over K = I
-            const uint32_t scb_all = 8u * (a.I / a.G) * 32u;
-            const int gper = a.I / a.G;
-            int dh[2][4], dl[2][4];  // two independent chains: chunk parity
-            int xs0 = 0, xs1 = 0;
-            bool fresh[2] = {true, true};
-#pragma unroll
-            for (int j = 0; j < W2C; ++j) {
-              const int c = hk * W2C + j;
-              const int par = j & 1;
-              const uint4 w = lds128(sbase + sidx * sb + (c * 32 + lane) * 16);
-#pragma unroll
-              for (int s2 = 0; s2 < 2; ++s2) {
-                uint32_t b[4];
-                load_b(xbase, rs, K, ld_row, ld_mat, 64 * c + 32 * s2, b);
-                uint32_t A[4];
-                unpack_u8(pick(w, 2 * s2), pick(w, 2 * s2 + 1), A);
-                if (s2 == 0 && fresh[par]) {
-                  imma_u8s8_zc(dh[par], A, b[0], b[1]);
-                  imma_u8u8_zc(dl[par], A, b[2], b[3]);
-                } else {
-                  imma_u8s8(dh[par], A, b[0], b[1]);
-                  imma_u8u8(dl[par], A, b[2], b[3]);
-                }
-              }
-              fresh[par] = false;
-              xs0 += meta.xsum[2 * t][c];
-              xs1 += meta.xsum[2 * t + 1][c];
-              if ((c + 1) % cpg == 0 || j == W2C - 1) {
-                const int grp = c / cpg;
-                const uint32_t scw = lds32(sbase + 8 * sb + ((sidx * gper + grp) * 8 + g) * 4);
-                const uint32_t zb =
-                    a.zero_mode == MTP_ZERO_RAW ? lds8(sbase + 8 * sb + scb_all + (sidx * gper + grp) * 8 + g) : 0x88u;
-                int z0, z1;
-                zero_rows_of(zb, a.zero_mode, z0, z1);
-                int sh[4], sl[4];
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                  sh[r] = (fresh[0] ? 0 : dh[0][r]) + (fresh[1] ? 0 : dh[1][r]);
-                  sl[r] = (fresh[0] ? 0 : dl[0][r]) + (fresh[1] ? 0 : dl[1][r]);
-                }
-                fold_int(acc, sh, sl, scw, z0, z1, xs0, xs1);
-                xs0 = xs1 = 0;
-                fresh[0] = fresh[1] = true;
-              }
-            }
-          }
-          if (!keep) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&cb.xempty[xb]));
-          }
-          if (hk == 1) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) red[(sidx * 4 + r) * 32 + lane] = acc[r];
-          }
-          named_bar_sync(kBarConsumers, kCT);
-          if (hk == 0) {
-            const int p0 = cols[2 * t], p1 = cols[2 * t + 1];
-            const float w0 = ((p0 >= 0 && p0 < a.numel) ? __ldcg(a.topk_w + p0) : 1.f) * meta.sx[2 * t];
-            const float w1 = ((p1 >= 0 && p1 < a.numel) ? __ldcg(a.topk_w + p1) : 1.f) * meta.sx[2 * t + 1];
-            const int nbase = 128 * idx + 16 * sidx;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              const int p = (r & 1) ? p1 : p0;
-              if (p >= 0) {
-                const float y = (acc[r] + red[(sidx * 4 + r) * 32 + lane]) * ((r & 1) ? w1 : w0);
-                a.ybuf[static_cast<int64_t>(p) * a.H + nbase + g + 8 * (r >> 1)] = y;
-              }
-            }
-          }
-          named_bar_sync(kBarConsumers, kCT);
-        }
-        if (!keep) {
-          if (++xb == 2) {
-            xb = 0;
-            xph ^= 1u;
-          }
+        umma_commit(smem_u32(&cb.dfull[ts]));
+        if (++ts == kTSlots) {
+          ts = 0;
+          tph ^= 1u;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&cb.empty[st]));
-      if (++st == a.stages) {
-        st = 0;
-        ph ^= 1u;
+      if (!keep) {
+        umma_commit(smem_u32(&cb.xempty[xb]));
+        if (++xb == 2) {
+          xb = 0;
+          xph ^= 1u;
+        }
       }
     }
   }
+  umma_commit(smem_u32(&cb.drain));
+  if (!mbar_wait(smem_u32(&cb.drain), 0, deadline)) record_timeout(a);
+}
 
-  // ------------------------- grid arrival + combine -------------------------
-  named_bar_sync(kBarConsumers, kCT);
-  if (ctid == 0 && !grid_sync(a, cb.gen0 + 2, deadline)) record_timeout(a);
-  named_bar_sync(kBarConsumers, kCT);
+// ---------------------------------------------------------------------------
+// epilogue warps (8-11)
+// ---------------------------------------------------------------------------
+template <int SK, int G>
+__device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, const OperandMeta* metas,
+                               const SlotScales* scales, float* xch, uint64_t deadline) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3;
+  const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
+  const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
+  constexpr int gps = SK / G, subs = kAccs / gps;
+  constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
+  int ts = 0, xb = 0;
+  uint32_t tph = 0;
+  int published = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const Pass P = make_pass(a, cb, table, pass);
+    const int K = pass == 0 ? a.H : a.I;
+    const int nst = K / SK;
+    for (int u = P.ub; u < P.ue; ++u) {
+      const int seg = u / P.per, b = u % P.per;
+      const int* e = ws_entry(P, seg);
+      const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
+      const OperandMeta& meta = metas[xb];
+      float acc[kFBM];
+#pragma unroll
+      for (int n = 0; n < kFBM; ++n) acc[n] = 0.f;
+      for (int s = 0; s < nst; ++s) {
+        if (!mbar_wait(smem_u32(&cb.dfull[ts]), tph, deadline) && lane == 0) record_timeout(a);
+        // the slot's scales come from the dequant warps through afull
+        if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline) && lane == 0) record_timeout(a);
+        tc_fence_after();
+        const uint32_t dt = cb.tmem + lane_addr + kTSlots * acols + ts * dcols;
+#pragma unroll
+        for (int g = 0; g < gps; ++g) {
+          // 256 * D_hi + D_lo' summed over the group's accumulators
+          int tsum[kFBM];
+#pragma unroll
+          for (int n = 0; n < kFBM; ++n) tsum[n] = 0;
+#pragma unroll
+          for (int j = 0; j < subs; ++j) {
+            uint32_t d[16];
+            tmem_ld16(dt + (g * subs + j) * 16, d);
+            tmem_wait_ld();
+#pragma unroll
+            for (int n = 0; n < kFBM; ++n) tsum[n] += 256 * static_cast<int>(d[n]) + static_cast<int>(d[8 + n]);
+          }
+          const SlotScales& ss = scales[ts];
+          const float sc = ss.s[g][r];
+          const int z = ss.z[g][r];
+          const int q128 = 128 * (static_cast<int>(ss.q[0][g][r]) + static_cast<int>(ss.q[1][g][r]));
+          const int gg = s * gps + g;
+#pragma unroll
+          for (int n = 0; n < kFBM; ++n) {
+            // sum_k (q - z) v = 256 D_hi + D_lo' + 128 sum q - z sum v
+            const int v = tsum[n] + q128 - z * meta.xsum[n][gg];
+            acc[n] = fmaf(static_cast<float>(v), sc, acc[n]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&cb.dempty[ts]));
+        if (++ts == kTSlots) {
+          ts = 0;
+          tph ^= 1u;
+        }
+      }
+      const int* cols = e + 4;
+      if (pass == 0) {
+        // rows 0-63 gate, 64-127 up: the up half hands its sums to the gate half
+        if (quad >= 2) {
+#pragma unroll
+          for (int n = 0; n < kFBM; ++n) xch[(r - 64) * kFBM + n] = acc[n];
+        }
+        named_bar_sync(kBarEpi, 128);
+        if (quad < 2) {
+#pragma unroll
+          for (int n = 0; n < kFBM; ++n) {
+            const int p = cols[n];
+            if (p >= 0) {
+              const float sx = meta.sx[n];
+              const float up = xch[r * kFBM + n] * sx;
+              a.hbuf[static_cast<int64_t>(p) * a.I + 64 * b + r] =
+                  __bfloat16_as_ushort(__float2bfloat16(silu(acc[n] * sx) * up));
+            }
+          }
+        }
+        // orders the h stores before the release below and protects xch
+        named_bar_sync(kBarEpi, 128);
+        ++published;
+        if (u + 1 == P.ue || (u + 1) / P.per != seg) {
+          if (threadIdx.x == kEpi0 * 32) red_release_gpu_add(a.seg_done + seg, published);
+          published = 0;
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < kFBM; ++n) {
+          const int p = cols[n];
+          if (p >= 0) {
+            const float w = (p < a.numel ? __ldcg(a.topk_w + p) : 1.f) * meta.sx[n];
+            a.ybuf[static_cast<int64_t>(p) * a.H + 128 * b + r] = acc[n] * w;
+          }
+        }
+      }
+      if (!keep) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&cb.xempty[xb]));
+        xb ^= 1;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int SK, int G>
+__global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
+  int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
+  uint8_t* stages = smem + kCtrlBytes + kTableBytes;
+  uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
+  OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
+  SlotScales* scales = reinterpret_cast<SlotScales*>(metas + 2);
+  float* xch = reinterpret_cast<float*>(scales + kTSlots);  // [64][kFBM]
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(smem_u32(&cb.full[i]), 1);
+      mbar_init(smem_u32(&cb.empty[i]), kDQ);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&cb.xfull[i]), 1);
+      mbar_init(smem_u32(&cb.xempty[i]), 1 + 4);
+      mbar_init(smem_u32(&cb.qfull[i]), 1);
+    }
+    for (int i = 0; i < kTSlots; ++i) {
+      mbar_init(smem_u32(&cb.afull[i]), kDQ);
+      mbar_init(smem_u32(&cb.dfull[i]), 1);
+      mbar_init(smem_u32(&cb.dempty[i]), 4);
+    }
+    mbar_init(smem_u32(&cb.drain), 1);
+    fence_mbar_init();
+    cb.gen0 = ld_acquire_gpu(a.bar + 1);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&cb.tmem), kTmemCols);
+    tmem_relinquish();
+  }
+  const uint64_t deadline = global_timer_ns() + kTimeoutNs;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // Phase 1: route this CTA's tokens (the stage ring is free scratch).
+  route_phase(a, reinterpret_cast<float*>(stages));
+  __syncthreads();
+  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 1, deadline)) record_timeout(a);
+  __syncthreads();
+  // Phase 2: the work-segment table of this CTA's unit ranges.
+  build_table(a, cb, table, reinterpret_cast<int*>(stages));
+  // Phase 3: the expert pipeline.
+  if (warp < kDQ) {
+    dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, scales, deadline);
+  } else if (warp < kEpi0 + 4) {
+    epilogue_warps<SK, G>(a, cb, table, metas, scales, xch, deadline);
+  } else if (warp == kMmaWarp) {
+    if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, deadline);
+    __syncwarp();
+  } else if (warp == kWProd) {
+    weight_producer(a, cb, table, stages, deadline);
+  } else if (warp == kBProd) {
+    operand_producer(a, cb, table, xbufs, deadline);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(cb.tmem, kTmemCols);
+  }
+  // ------------------------- grid barrier + combine -------------------------
+  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 2, deadline)) record_timeout(a);
+  __syncthreads();
   // The per-call counters are no longer read by anyone: zero them for the
   // next call, a slice per CTA.
   {
     const int G = gridDim.x, c = blockIdx.x;
-    for (int i = a.E * c / G + ctid; i < a.E * (c + 1) / G; i += kCT) a.cnt[i] = 0;
-    for (int i = cb.S * c / G + ctid; i < cb.S * (c + 1) / G; i += kCT) a.seg_done[i] = 0;
+    for (int i = a.E * c / G + threadIdx.x; i < a.E * (c + 1) / G; i += kThreads) a.cnt[i] = 0;
+    for (int i = cb.S * c / G + threadIdx.x; i < cb.S * (c + 1) / G; i += kThreads) a.seg_done[i] = 0;
   }
   const int quads = a.H / 4;
   const int64_t total = static_cast<int64_t>(a.M) * quads;
   const int64_t b = total * blockIdx.x / gridDim.x, e = total * (blockIdx.x + 1) / gridDim.x;
-  for (int64_t i = b + ctid; i < e; i += kCT) {
+  for (int64_t i = b + threadIdx.x; i < e; i += kThreads) {
     const int tok = static_cast<int>(i / quads);
     const int n = static_cast<int>(i % quads) * 4;
     float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -953,66 +1083,29 @@ __device__ void consumers(const FusedArgs& a, Ctrl& cb, const int* table, uint8_
   }
 }
 
-template <int W1C, int W2C>
-__global__ void __launch_bounds__(kFusedThreads, 1) moe_fused_kernel(FusedArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
-  int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
-  uint8_t* stages = smem + kCtrlBytes + kTableBytes;
-  uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
-  OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
-  float* red = reinterpret_cast<float*>(metas + 2);
-  const int warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < a.stages; ++i) {
-      mbar_init(smem_u32(&cb.full[i]), 1);
-      mbar_init(smem_u32(&cb.empty[i]), kCW);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&cb.xfull[i]), 1);
-      mbar_init(smem_u32(&cb.xempty[i]), kCW);
-    }
-    fence_mbar_init();
-  }
-  if (threadIdx.x == 0) cb.gen0 = ld_acquire_gpu(a.bar + 1);
-  const uint64_t deadline = global_timer_ns() + kTimeoutNs;
-  __syncthreads();
-  // Phase 1: route this CTA's tokens (the stage ring is free scratch).
-  if (warp < kCW) route_phase(a, threadIdx.x, reinterpret_cast<float*>(stages));
-  __syncthreads();
-  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 1, deadline)) record_timeout(a);
-  __syncthreads();
-  // Phase 2: the work-segment table of this CTA's unit ranges.
-  build_table(a, cb, table, reinterpret_cast<int*>(stages));
-  __syncthreads();
-  if (warp == kWProd) {
-    weight_producer(a, cb, table, stages, deadline);
-  } else if (warp == kBProd) {
-    operand_producer(a, cb, table, xbufs, deadline);
-  } else {
-    consumers<W1C, W2C>(a, cb, table, stages, xbufs, metas, red, deadline);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct FusedGeometry {
-  int stages;
+  int stages, sk;
   uint32_t stage_bytes, xbuf_bytes;
   size_t smem;
 };
 
 static uint32_t round128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
 
+// K per stage: 256 when it divides both H and I, else 128.
+static int stage_k(int H, int I) { return (H % 256 == 0 && I % 256 == 0) ? 256 : 128; }
+
 static FusedGeometry fused_geometry(int H, int I, int G) {
   FusedGeometry f;
-  const uint64_t w1 = 16ull * H + 2ull * (H / G) * 32 + 2ull * (H / G) * 8;
-  const uint64_t w2 = 64ull * I + 8ull * (I / G) * 32 + 8ull * (I / G) * 8;
-  f.stage_bytes = round128(w1 > w2 ? w1 : w2);
+  f.sk = stage_k(H, I);
+  const int gps = f.sk / G;
+  f.stage_bytes = round128(static_cast<uint64_t>(f.sk) * 64 + gps * 256 + gps * 64);
   const int maxrow = H > I ? H : I;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (2ull * maxrow + 16));
-  const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2ull * sizeof(OperandMeta) + kRedBytes;
+  const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
+                       kTSlots * sizeof(SlotScales) + 64 * kFBM * sizeof(float);
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;
@@ -1034,47 +1127,37 @@ static int device_sms() {
   return cached_sms;
 }
 
-template <int W1C, int W2C>
-static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream_t st) {
-  static int configured = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured != dev) {
-    if (cudaFuncSetAttribute(moe_fused_kernel<W1C, W2C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024) != cudaSuccess)
-      return MTP_ERR_CUDA;
-    configured = dev;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(device_sms());
-  cfg.blockDim = dim3(kFusedThreads);
-  cfg.dynamicSmemBytes = f.smem;
-  cfg.stream = st;
-  cfg.attrs = nullptr;
-  cfg.numAttrs = 0;
-  if (cudaLaunchKernelEx(&cfg, moe_fused_kernel<W1C, W2C>, a) != cudaSuccess) return MTP_ERR_LAUNCH;
-  return MTP_OK;
-}
-
-// W1C: 64-wide K chunks per W1 warp (H/64 chunks over at most 16 warps);
-// W2C: chunks per W2 warp (two warps per strip split K = I).
-static bool fused_template(int H, int I, int* w1c, int* w2c) {
-  *w1c = H > 1024 ? 2 : 1;
-  *w2c = I / 128;
-  return (H / 64) % *w1c == 0 && H / 64 / *w1c <= kCW && *w2c >= 1 && *w2c <= 8;
-}
 
 bool fused_supported(int H, int I, int G) {
   if (G != 64 && G != 128) return false;
-  if (H % 128 || I % 128 || H % G || I % G) return false;
-  int w1c, w2c;
-  if (!fused_template(H, I, &w1c, &w2c)) return false;
-  return fused_geometry(H, I, G).stages >= 2;
+  if (H % 256 || I % 128 || H > 2048 || I > 1024 || H % G || I % G) return false;
+  const FusedGeometry f = fused_geometry(H, I, G);
+  if (f.sk % G) return false;
+  // tensor memory: kTSlots x (A tile + accumulators) <= 512 columns; every
+  // group of a stage gets a whole number of the kAccs accumulators
+  if (kTSlots * (f.sk / 4 + kAccs * 16) > kTmemCols) return false;
+  if (f.sk / G > kAccs || kAccs % (f.sk / G) || (G / 32) % (kAccs / (f.sk / G))) return false;
+  return f.stages >= 4;
 }
 
 int fused_max_work_segments(int M, int max_seg, int max_blocks) {
   const int shared_blocks = (M + kFBM - 1) / kFBM;
   return max_seg + max_blocks / kWsBlocks + (shared_blocks + kWsBlocks - 1) / kWsBlocks + 2;
+}
+
+template <int SK, int G>
+static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream_t st) {
+  static int configured = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MTP_ERR_CUDA;
+  if (configured != dev) {
+    if (cudaFuncSetAttribute(moe_fused_kernel<SK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+        cudaSuccess)
+      return MTP_ERR_CUDA;
+    configured = dev;
+  }
+  moe_fused_kernel<SK, G><<<device_sms(), kThreads, f.smem, st>>>(a);
+  return launch_status();
 }
 
 int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {
@@ -1083,27 +1166,11 @@ int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {
   a.stages = f.stages;
   a.stage_bytes = f.stage_bytes;
   a.xbuf_bytes = f.xbuf_bytes;
-  int w1c, w2c;
-  fused_template(a.H, a.I, &w1c, &w2c);
-#define MTP_FUSED_CASE(A, B) \
-  if (w1c == A && w2c == B) return launch_fused_t<A, B>(a, f, st);
-  MTP_FUSED_CASE(1, 1)
-  MTP_FUSED_CASE(1, 2)
-  MTP_FUSED_CASE(1, 3)
-  MTP_FUSED_CASE(1, 4)
-  MTP_FUSED_CASE(1, 5)
-  MTP_FUSED_CASE(1, 6)
-  MTP_FUSED_CASE(1, 7)
-  MTP_FUSED_CASE(1, 8)
-  MTP_FUSED_CASE(2, 1)
-  MTP_FUSED_CASE(2, 2)
-  MTP_FUSED_CASE(2, 3)
-  MTP_FUSED_CASE(2, 4)
-  MTP_FUSED_CASE(2, 5)
-  MTP_FUSED_CASE(2, 6)
-  MTP_FUSED_CASE(2, 7)
-  MTP_FUSED_CASE(2, 8)
-#undef MTP_FUSED_CASE
+  a.sk = f.sk;
+  if (f.sk == 256 && a.G == 128) return launch_fused_t<256, 128>(a, f, st);
+  if (f.sk == 256 && a.G == 64) return launch_fused_t<256, 64>(a, f, st);
+  if (f.sk == 128 && a.G == 128) return launch_fused_t<128, 128>(a, f, st);
+  if (f.sk == 128 && a.G == 64) return launch_fused_t<128, 64>(a, f, st);
   return MTP_ERR_SHAPE;
 }
 

@@ -31,37 +31,40 @@ def expert_layout(hidden: int, inter: int, group: int) -> dict[str, int]:
     return off
 
 
-def repack_projection(qweight: np.ndarray, qzeros: np.ndarray, scales: np.ndarray, group: int):
+def block_rows(n: int, gated: bool) -> np.ndarray:
+    """[n/128, 128] source row of each row of each 128-row block: for a gated
+    projection (w13, n = 2I) block b is gate rows 64b..64b+63 then up rows
+    I+64b..I+64b+63; otherwise rows 128b..128b+127."""
+    nb = n // 128
+    r = np.arange(128)
+    if gated:
+        half = n // 2
+        return np.stack([np.where(r < 64, 64 * b + r, half + 64 * b + (r - 64)) for b in range(nb)])
+    return np.stack([128 * b + r for b in range(nb)])
+
+
+def repack_projection(qweight: np.ndarray, qzeros: np.ndarray, scales: np.ndarray, group: int,
+                      gated: bool = False):
     """GPTQ [K/8, N] / [K/G, N/8] / [K/G, N] -> (weights bytes, scales bytes, zeros bytes)."""
     q = gptq.unpack_rows(qweight)            # [K, N] values 0..15
     z = gptq.unpack_cols(qzeros)             # [K/G, N]
     s = np.ascontiguousarray(scales).view(np.uint16)  # [K/G, N]
     k, n = q.shape
-    strips, chunks, groups = n // 16, k // 64, k // group
-    # words[s, c, lane, kk]: row 16s + g + 8(kk & 1), k base 64c + 32(kk >> 1) + 4t;
-    # byte b = q(row, kb + b) | q(row, kb + 16 + b) << 4
-    lane = np.arange(32)
-    g, t = lane // 4, lane % 4
-    words = np.zeros((strips, chunks, 32, 4), dtype=np.uint32)
-    for si in range(strips):
-        for c in range(chunks):
-            for kk in range(4):
-                r = 16 * si + g + 8 * (kk & 1)
-                kb = 64 * c + 32 * (kk >> 1) + 4 * t
-                w = np.zeros(32, dtype=np.uint32)
-                for b in range(4):
-                    byte = q[kb + b, r].astype(np.uint32) | (q[kb + 16 + b, r].astype(np.uint32) << np.uint32(4))
-                    w |= byte << np.uint32(8 * b)
-                words[si, c, :, kk] = w
-    sc = np.zeros((strips, groups, 8, 2), dtype=np.uint16)
-    zp = np.zeros((strips, groups, 8), dtype=np.uint8)
-    for si in range(strips):
-        for gr in range(groups):
-            rows = 16 * si + np.arange(8)
-            sc[si, gr, :, 0] = s[gr, rows]
-            sc[si, gr, :, 1] = s[gr, rows + 8]
-            zp[si, gr, :] = (z[gr, rows] | (z[gr, rows + 8] << 4)).astype(np.uint8)
-    return words.view(np.uint8).reshape(-1), sc.view(np.uint8).reshape(-1), zp.reshape(-1)
+    rows = block_rows(n, gated)              # [nb, 128]
+    nb, chunks, groups = n // 128, k // 32, k // group
+    # words[b, c, r, j]: k0 = 32c + 8j; byte t = q(k0 + t) | q(k0 + 4 + t) << 4
+    qt = q.T.astype(np.uint32)               # [N, K]
+    qb = qt[rows]                            # [nb, 128, K]
+    qb = qb.reshape(nb, 128, chunks, 4, 2, 4)  # [.., c, j, half, t]: k = 32c + 8j + 4 half + t
+    lo, hi = qb[..., 0, :], qb[..., 1, :]      # [nb, 128, c, j, t]
+    shifts = (8 * np.arange(4)).astype(np.uint32)
+    words = ((lo | (hi << np.uint32(4))) << shifts).sum(axis=-1).astype(np.uint32)  # [nb, 128, c, j]
+    words = words.transpose(0, 2, 1, 3)      # [nb, c, 128, j]
+    sc = s.T[rows].transpose(0, 2, 1)        # [nb, groups, 128]
+    zt = z.T[rows].transpose(0, 2, 1).astype(np.uint8)  # [nb, groups, 128]
+    zp = (zt[..., 0::2] | (zt[..., 1::2] << 4)).astype(np.uint8)  # [nb, groups, 64]
+    return (np.ascontiguousarray(words).view(np.uint8).reshape(-1),
+            np.ascontiguousarray(sc).view(np.uint8).reshape(-1), np.ascontiguousarray(zp).reshape(-1))
 
 
 def repack_expert(t: dict, e: int | None, hidden: int, inter: int, group: int) -> np.ndarray:
@@ -72,7 +75,8 @@ def repack_expert(t: dict, e: int | None, hidden: int, inter: int, group: int) -
     L = expert_layout(hidden, inter, group)
     blob = np.zeros(L["bytes"], dtype=np.uint8)
     for p in ("w13", "w2"):
-        qw, sc, zp = repack_projection(get(f"{p}_qweight"), get(f"{p}_qzeros"), get(f"{p}_scales"), group)
+        qw, sc, zp = repack_projection(get(f"{p}_qweight"), get(f"{p}_qzeros"), get(f"{p}_scales"), group,
+                                       gated=(p == "w13"))
         blob[L[f"{p}_qweight"]:L[f"{p}_qweight"] + qw.size] = qw
         blob[L[f"{p}_scales"]:L[f"{p}_scales"] + sc.size] = sc
         blob[L[f"{p}_zeros"]:L[f"{p}_zeros"] + zp.size] = zp
@@ -80,30 +84,25 @@ def repack_expert(t: dict, e: int | None, hidden: int, inter: int, group: int) -
 
 
 def decode_projection(blob: np.ndarray, off_q: int, off_s: int, off_z: int, n: int, k: int, group: int,
-                      zero_mode: str = "raw") -> np.ndarray:
+                      zero_mode: str = "raw", gated: bool = False) -> np.ndarray:
     """Inverse: kernel layout -> fp32 [N, K] (Linear orientation), computed as the
     kernel's dequantisation defines it: (q - z) * s per element."""
-    strips, chunks, groups = n // 16, k // 64, k // group
-    words = blob[off_q:off_q + n * k // 2].view(np.uint32).reshape(strips, chunks, 32, 4)
-    sc = blob[off_s:off_s + n * groups * 2].view(np.float16).reshape(strips, groups, 8, 2)
-    zp = blob[off_z:off_z + n * groups // 2].reshape(strips, groups, 8)
+    nb, chunks, groups = n // 128, k // 32, k // group
+    words = blob[off_q:off_q + n * k // 2].view(np.uint32).reshape(nb, chunks, 128, 4)
+    sc = blob[off_s:off_s + n * groups * 2].view(np.float16).reshape(nb, groups, 128).astype(np.float32)
+    zp = blob[off_z:off_z + n * groups // 2].reshape(nb, groups, 64)
+    zr = np.empty((nb, groups, 128), dtype=np.float32)
+    zr[..., 0::2] = zp & 0xF
+    zr[..., 1::2] = zp >> 4
+    if zero_mode == "sym8":
+        zr[:] = 8.0
+    t = np.arange(4, dtype=np.uint32)
+    lo = (words[..., None] >> (8 * t)) & np.uint32(0xF)           # [nb, c, 128, j, t]
+    hi = (words[..., None] >> (8 * t + 4)) & np.uint32(0xF)
+    q = np.stack([lo, hi], axis=-2).astype(np.float32)             # [nb, c, 128, j, half, t]
+    q = q.transpose(0, 2, 1, 3, 4, 5).reshape(nb, 128, k)          # k = 32c + 8j + 4 half + t
+    gidx = np.arange(k) // group
+    deq = (q - zr.transpose(0, 2, 1)[:, :, gidx]) * sc.transpose(0, 2, 1)[:, :, gidx]
     out = np.zeros((n, k), dtype=np.float32)
-    lane = np.arange(32)
-    g, t = lane // 4, lane % 4
-    for si in range(strips):
-        for c in range(chunks):
-            for kk in range(4):
-                w = words[si, c, :, kk]
-                rr = 16 * si + g + 8 * (kk & 1)
-                kb = 64 * c + 32 * (kk >> 1) + 4 * t
-                for b in range(4):
-                    byte = (w >> np.uint32(8 * b)) & np.uint32(0xFF)
-                    for kc, qv in ((kb + b, byte & np.uint32(0xF)), (kb + 16 + b, byte >> np.uint32(4))):
-                        grp = kc // group
-                        zbyte = zp[si, grp, g]
-                        zrow = np.where((kk & 1) == 0, zbyte & 0xF, zbyte >> 4).astype(np.float32)
-                        if zero_mode == "sym8":
-                            zrow = np.float32(8.0)
-                        srow = np.where((kk & 1) == 0, sc[si, grp, g, 0], sc[si, grp, g, 1]).astype(np.float32)
-                        out[rr, kc] = (qv.astype(np.float32) - zrow) * srow
+    out[block_rows(n, gated).reshape(-1)] = deq.reshape(nb * 128, k)
     return out

@@ -14,7 +14,8 @@ def test_layout_decode_equals_gptq_dequant():
     L = layout.expert_layout(h, i, gs)
     for e in (0, 3, 7):
         blob = layout.repack_expert(ex, e, h, i, gs)
-        w13 = layout.decode_projection(blob, L["w13_qweight"], L["w13_scales"], L["w13_zeros"], 2 * i, h, gs)
+        w13 = layout.decode_projection(blob, L["w13_qweight"], L["w13_scales"], L["w13_zeros"], 2 * i, h, gs,
+                                       gated=True)
         w2 = layout.decode_projection(blob, L["w2_qweight"], L["w2_scales"], L["w2_zeros"], h, i, gs)
         ref13 = gptq.dequantize(ex["w13_qweight"][e].numpy(), ex["w13_qzeros"][e].numpy(), ex["w13_scales"][e].numpy())
         ref2 = gptq.dequantize(ex["w2_qweight"][e].numpy(), ex["w2_qzeros"][e].numpy(), ex["w2_scales"][e].numpy())
