@@ -202,7 +202,7 @@ MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
  * address (with that device current), so make it before any stream capture.
  * All calls share the array and it keeps the last call's contents; calls that
  * overlap on the GPU race and must be serialised by the caller.            */
-#define MTP_NOALLOC_SCRATCH_BYTES (5u << 20)
+#define MTP_NOALLOC_SCRATCH_BYTES (6u << 20)
 MTP_API int mtp_w4a16_moe_layer_noalloc(const MtpMoeLayerArgs* args, void* stream);
 
 #ifdef __cplusplus

@@ -126,6 +126,8 @@ __device__ __forceinline__ float bf16_bits_to_float(uint16_t v) {
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x) with a fast reciprocal (-> 0 for very negative x)
+__device__ __forceinline__ float silu_fast(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
 
 // Warp reductions
 __device__ __forceinline__ float warp_sum(float v) {

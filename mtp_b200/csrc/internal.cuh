@@ -31,11 +31,14 @@ struct FusedArgs {
   const uint8_t* host_blobs;
   const uint8_t* shared_blob;
   float* gate;               // [M] sigmoid(x . w_g)
+  uint8_t* xq;               // [M][2H] quantised x: H high bytes, H offset low bytes
+  float* xsx;                // [M] row scale of xq
+  int32_t* xsq;              // [M][H/G] group sums of the 16-bit values
   int32_t* bar;              // [2] grid barrier (count, generation)    \ zero before the first
   int32_t* cnt;              // [E] pairs per expert                    |  call; every call
   int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero
   int32_t* lists;            // [E][M] pair ids per expert
-  uint16_t* hbuf;
+  float* gu;                 // [numel + M][2I] fp32 W1 sums per pair: gate | up
   float* ybuf;
   uint16_t* out;
   float* out_f32;

@@ -309,6 +309,60 @@ __device__ __forceinline__ void router_warp(const float* __restrict__ row, int E
   *id_out = my_id;
 }
 
+// 16-bit integers v -> the high bytes and the offset low bytes (v & 255) ^ 128
+// (= lo - 128 as a signed byte) of four values, packed little-endian.
+__device__ __forceinline__ void pack_hilo(int v0, int v1, int v2, int v3, uint32_t& hw, uint32_t& lw) {
+  hw = __byte_perm(__byte_perm(v0, v1, 0x0051), __byte_perm(v2, v3, 0x0051), 0x5410);
+  lw = __byte_perm(__byte_perm(v0, v1, 0x0040), __byte_perm(v2, v3, 0x0040), 0x5410) ^ 0x80808080u;
+}
+
+// Quantise one token's x row (one warp, lane holding the 8-element vectors
+// lane + 32 j) to 16-bit integers v = round(x / sx), sx = max|x| / 32767, and
+// store them as a high-byte row then an offset low-byte row (xq[t] = 2H
+// bytes), with sx and the per-group sums of v (xsq[t][H / G]).
+__device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const uint4 (&xv)[8]) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.H / 8;
+  float mx = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (lane + 32 * j < nvec) {
+      const uint32_t m = __vmaxu2(__vmaxu2(xv[j].x & 0x7fff7fffu, xv[j].y & 0x7fff7fffu),
+                                  __vmaxu2(xv[j].z & 0x7fff7fffu, xv[j].w & 0x7fff7fffu));
+      mx = fmaxf(mx, fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u)));
+    }
+  }
+  mx = warp_max(mx);
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  uint8_t* row = a.xq + static_cast<int64_t>(t) * 2 * a.H;
+  const int lpg = a.G / 8;  // lanes (8-element vectors) per group: 8 or 16
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    int sum = 0;
+    if (lane + 32 * j < nvec) {
+      const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      int v[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[2 * e] = __float2int_rn(__uint_as_float(w[e] << 16) * inv);
+        v[2 * e + 1] = __float2int_rn(__uint_as_float(w[e] & 0xffff0000u) * inv);
+      }
+      uint2 hi, lo;
+      pack_hilo(v[0], v[1], v[2], v[3], hi.x, lo.x);
+      pack_hilo(v[4], v[5], v[6], v[7], hi.y, lo.y);
+      const int vi = lane + 32 * j;
+      *reinterpret_cast<uint2*>(row + 8 * vi) = hi;
+      *reinterpret_cast<uint2*>(row + a.H + 8 * vi) = lo;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[e];
+    }
+    // a group is lpg consecutive lanes of one j
+    for (int o = 1; o < lpg; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
+    if ((lane & (lpg - 1)) == 0 && lane + 32 * j < nvec) a.xsq[static_cast<int64_t>(t) * (a.H / a.G) + (lane + 32 * j) / lpg] = sum;
+  }
+  if (lane == 0) a.xsx[t] = mx / 32767.f;
+}
+
 // Phase 1: route this CTA's tokens, count and list the (token, slot) pairs per
 // expert, and compute the shared-expert gate. Warps 0-6 route a token each;
 // warps 7-13 compute the gates of the same tokens. `scratch` holds 7 x E
@@ -341,35 +395,39 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
         if (pos < a.M) a.lists[static_cast<int64_t>(id) * a.M + pos] = t * a.k + lane;
         else atomicOr(a.status + 2, 4);
       }
-    } else if (a.has_shared) {
-      // sigmoid(x . w_g): all of a lane's 16-byte loads in flight at once
+    } else {
+      // The token's x row, all of a lane's 16-byte loads in flight at once:
+      // quantised once for every expert that uses it (see quantize_token), and
+      // sigmoid(x . w_g) for the shared expert.
       const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(t) * a.H);
-      const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
       const int nvec = a.H / 8;  // <= 256: at most 8 per lane
-      uint4 xv[8], wv[8];
+      uint4 xv[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int vi = lane + 32 * j;
-        if (vi < nvec) {
-          xv[j] = xr[vi];
-          wv[j] = wg[vi];
-        }
-      }
-      float part = 0.f;
+      for (int j = 0; j < 8; ++j)
+        if (lane + 32 * j < nvec) xv[j] = xr[lane + 32 * j];
+      quantize_token(a, t, xv);
+      if (a.has_shared) {
+        const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
+        uint4 wv[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (lane + 32 * j < nvec) {
-          const uint32_t* xs = reinterpret_cast<const uint32_t*>(&xv[j]);
-          const uint32_t* ws = reinterpret_cast<const uint32_t*>(&wv[j]);
+        for (int j = 0; j < 8; ++j)
+          if (lane + 32 * j < nvec) wv[j] = wg[lane + 32 * j];
+        float part = 0.f;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            part = fmaf(__uint_as_float(xs[q] << 16), __uint_as_float(ws[q] << 16), part);
-            part = fmaf(__uint_as_float(xs[q] & 0xffff0000u), __uint_as_float(ws[q] & 0xffff0000u), part);
+        for (int j = 0; j < 8; ++j) {
+          if (lane + 32 * j < nvec) {
+            const uint32_t* xs = reinterpret_cast<const uint32_t*>(&xv[j]);
+            const uint32_t* ws = reinterpret_cast<const uint32_t*>(&wv[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              part = fmaf(__uint_as_float(xs[q] << 16), __uint_as_float(ws[q] << 16), part);
+              part = fmaf(__uint_as_float(xs[q] & 0xffff0000u), __uint_as_float(ws[q] & 0xffff0000u), part);
+            }
           }
         }
+        part = warp_sum(part);
+        if (lane == 0) a.gate[t] = 1.f / (1.f + expf(-part));
       }
-      part = warp_sum(part);
-      if (lane == 0) a.gate[t] = 1.f / (1.f + expf(-part));
     }
   }
 }
@@ -584,11 +642,15 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
 __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs,
                                  uint64_t deadline) {
   const int lane = threadIdx.x & 31;
+  // the quantised x rows were written with ordinary stores in the routing
+  // phase; order them before this thread's bulk (async proxy) reads
+  fence_proxy_async_global();
   int xb = 0;
   uint32_t xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
-    const uint32_t row_bytes = pass == 0 ? 2u * a.H : 2u * a.I;
+    // W1: quantised x rows (2H bytes); W2: fp32 gate|up rows (8I bytes)
+    const uint32_t row_bytes = pass == 0 ? 2u * a.H : 8u * a.I;
     const uint32_t row_stride = row_bytes + 16u;
     int waited_seg = -1;
     for (int u = P.ub; u < P.ue; ++u) {
@@ -621,8 +683,8 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
       __syncwarp();
       if (p >= 0) {
         const uint8_t* src = pass == 0
-                                 ? reinterpret_cast<const uint8_t*>(a.x + static_cast<int64_t>(pair_token(a, p)) * a.H)
-                                 : reinterpret_cast<const uint8_t*>(a.hbuf + static_cast<int64_t>(p) * a.I);
+                                 ? a.xq + static_cast<int64_t>(pair_token(a, p)) * 2 * a.H
+                                 : reinterpret_cast<const uint8_t*>(a.gu + static_cast<int64_t>(p) * 2 * a.I);
         bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
       }
       if (++xb == 2) {
@@ -636,28 +698,74 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
 // ---------------------------------------------------------------------------
 // dequant warps (0-7): operand quantisation and the A tiles in tensor memory
 // ---------------------------------------------------------------------------
-// Quantise the 8 bf16 rows of an operand buffer in place into 16-bit integers
-// v = 256 * hi + lo' + 128 laid out as the MMA's B operand: the signed high
-// bytes hi at [0, 8K), the signed offset low bytes lo' = (v & 255) - 128 at
-// [8K, 16K), each plane K-major in 8-row x 16-byte core matrices ((n, k) at
-// (k / 16) * 128 + n * 16 + k % 16), so one N=16 MMA covers both planes; one
-// scale per row and per-group sums of v. Thread (warp w, lane = 4n + q)
-// owns the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i, so every
-// plane store of a warp is one contiguous 128-byte core matrix. All values
-// are read before the first barrier and written after it (the output
-// overlaps the input).
+// W1 operand: the 8 token rows arrive already quantised (xq rows: K high
+// bytes then K offset low bytes, see quantize_token); rearrange them in place
+// into the MMA's B layout, both planes K-major in 8-row x 16-byte core
+// matrices ((n, k) at (k / 16) * 128 + n * 16 + k % 16, high plane at [0, 8K),
+// low plane at [8K, 16K)), and fetch each row's scale and group sums. Thread
+// t moves the 16-byte pieces t + 256 i (row fastest), so both the reads and
+// the writes of a warp are conflict-free. All pieces are read before the
+// barrier and written after it (the output overlaps the input).
 template <int G>
-__device__ __forceinline__ void quantize_rows(uint8_t* rows, OperandMeta& meta, int K) {
+__device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* pairs, uint8_t* rows,
+                                                OperandMeta& meta) {
+  const int t = threadIdx.x, K = a.H;
+  const int pieces = 2 * (K / 16) * kFBM;  // <= 2048: at most 8 per thread
+  uint4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int pc = t + kDQ * 32 * i;
+    if (pc < pieces) {
+      const int n = pc & 7, cc = pc >> 3;  // cc over both planes: plane = cc / (K / 16)
+      v[i] = *reinterpret_cast<const uint4*>(rows + n * (2 * K + 16) + cc * 16);
+    }
+  }
+  if (t < kFBM * (K / G)) {
+    const int n = t / (K / G), g = t % (K / G);
+    const int p = pairs[n];
+    meta.xsum[n][g] = p >= 0 ? __ldcg(a.xsq + static_cast<int64_t>(pair_token(a, p)) * (K / G) + g) : 0;
+  }
+  if (t < kFBM) {
+    const int p = pairs[t];
+    meta.sx[t] = p >= 0 ? __ldcg(a.xsx + pair_token(a, p)) : 0.f;
+  }
+  named_bar_sync(kBarDequant, kDQ * 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int pc = t + kDQ * 32 * i;
+    if (pc < pieces) {
+      const int n = pc & 7, cc = pc >> 3;
+      const int plane = cc / (K / 16), c = cc % (K / 16);
+      *reinterpret_cast<uint4*>(rows + plane * 8 * K + c * 128 + n * 16) = v[i];
+    }
+  }
+  fence_proxy_async_shared();  // the planes are read by the tensor cores
+  named_bar_sync(kBarDequant, kDQ * 32);
+}
+
+// W2 operand: the 8 pair rows arrive as fp32 W1 sums (K gate values, then K up
+// values); form h = bf16(silu(gate) * up) and quantise it in place to 16-bit
+// integers v = 256 * hi + lo' + 128, laid out as the B planes above, with one
+// scale per row and per-group sums of v. Thread (warp w, lane = 4n + q) owns
+// the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i.
+template <int G>
+__device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta, int K) {
   const int t = threadIdx.x, w = t >> 5, lane = t & 31, n = lane >> 2, q = lane & 3;
-  const int iters = K / 128;  // <= 16
-  const uint8_t* row = rows + n * (2 * K + 16);
-  uint2 raw[16];
+  const int iters = K / 128;  // <= 8
+  const uint8_t* row = rows + n * (8 * K + 16);
+  uint2 raw[8];
   float mx = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     raw[i] = make_uint2(0u, 0u);
     if (i < iters) {
-      raw[i] = *reinterpret_cast<const uint2*>(row + 2 * (16 * (w + 8 * i) + 4 * q));
+      const int k0 = 16 * (w + 8 * i) + 4 * q;
+      const float4 g = *reinterpret_cast<const float4*>(row + 4 * k0);
+      const float4 u = *reinterpret_cast<const float4*>(row + 4 * (K + k0));
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(silu_fast(g.x) * u.x, silu_fast(g.y) * u.y);
+      const __nv_bfloat162 h23 = __floats2bfloat162_rn(silu_fast(g.z) * u.z, silu_fast(g.w) * u.w);
+      raw[i].x = *reinterpret_cast<const uint32_t*>(&h01);
+      raw[i].y = *reinterpret_cast<const uint32_t*>(&h23);
       const uint32_t m0 = __vmaxu2(raw[i].x & 0x7fff7fffu, raw[i].y & 0x7fff7fffu);
       mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
     }
@@ -671,25 +779,20 @@ __device__ __forceinline__ void quantize_rows(uint8_t* rows, OperandMeta& meta, 
 #pragma unroll
   for (int j = 0; j < kDQ; ++j) amax = fmaxf(amax, meta.amax[j][n]);
   const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-  uint8_t* hi_plane = rows;
-  uint8_t* lo_plane = rows + 8 * K;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     if (i < iters) {  // warp-uniform
       const int cc = w + 8 * i;
-      uint32_t hw = 0u, lw = 0u;
-      int sum = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t h = (b < 2 ? raw[i].x : raw[i].y) >> (16 * (b & 1));
-        const int v = max(-32767, min(32767, __float2int_rn(__uint_as_float(h << 16) * inv)));
-        sum += v;
-        hw |= (static_cast<uint32_t>(v >> 8) & 0xffu) << (8 * b);
-        lw |= ((static_cast<uint32_t>(v) & 0xffu) ^ 0x80u) << (8 * b);
-      }
+      const int v0 = __float2int_rn(__uint_as_float(raw[i].x << 16) * inv);
+      const int v1 = __float2int_rn(__uint_as_float(raw[i].x & 0xffff0000u) * inv);
+      const int v2 = __float2int_rn(__uint_as_float(raw[i].y << 16) * inv);
+      const int v3 = __float2int_rn(__uint_as_float(raw[i].y & 0xffff0000u) * inv);
+      uint32_t hw, lw;
+      pack_hilo(v0, v1, v2, v3, hw, lw);
       const int off = cc * 128 + n * 16 + 4 * q;
-      *reinterpret_cast<uint32_t*>(hi_plane + off) = hw;
-      *reinterpret_cast<uint32_t*>(lo_plane + off) = lw;
+      *reinterpret_cast<uint32_t*>(rows + off) = hw;
+      *reinterpret_cast<uint32_t*>(rows + 8 * K + off) = lw;
+      int sum = v0 + v1 + v2 + v3;
       sum += __shfl_xor_sync(kFullMask, sum, 1);
       sum += __shfl_xor_sync(kFullMask, sum, 2);
       if (q == 0) atomicAdd(&meta.xsum[n][(16 * cc) / G], sum);
@@ -724,7 +827,10 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
       const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
       if (!reuse) {
         if (!mbar_wait(smem_u32(&cb.xfull[xb]), xph, deadline) && threadIdx.x == 0) record_timeout(a);
-        quantize_rows<G>(xbufs + xb * a.xbuf_bytes, metas[xb], K);
+        if (pass == 0)
+          relayout_x_rows<G>(a, ws_entry(P, u / P.per) + 4, xbufs + xb * a.xbuf_bytes, metas[xb]);
+        else
+          quantize_h_rows<G>(xbufs + xb * a.xbuf_bytes, metas[xb], K);
         if (threadIdx.x == 0) mbar_arrive(smem_u32(&cb.qfull[xb]));
       }
       for (int s = 0; s < nst; ++s) {
@@ -861,7 +967,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, const OperandMeta* metas,
-                               const SlotScales* scales, float* xch, uint64_t deadline) {
+                               const SlotScales* scales, uint64_t deadline) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
@@ -925,28 +1031,18 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
       }
       const int* cols = e + 4;
       if (pass == 0) {
-        // rows 0-63 gate, 64-127 up: the up half hands its sums to the gate half
-        if (quad >= 2) {
+        // gate rows 0-63 and up rows 64-127 of block b: fp32 sums per pair;
+        // silu(gate) * up is formed when the W2 operand is loaded
+        const int row = r < 64 ? 64 * b + r : a.I + 64 * b + (r - 64);
 #pragma unroll
-          for (int n = 0; n < kFBM; ++n) xch[(r - 64) * kFBM + n] = acc[n];
+        for (int n = 0; n < kFBM; ++n) {
+          const int p = cols[n];
+          if (p >= 0) a.gu[static_cast<int64_t>(p) * 2 * a.I + row] = acc[n] * meta.sx[n];
         }
-        named_bar_sync(kBarEpi, 128);
-        if (quad < 2) {
-#pragma unroll
-          for (int n = 0; n < kFBM; ++n) {
-            const int p = cols[n];
-            if (p >= 0) {
-              const float sx = meta.sx[n];
-              const float up = xch[r * kFBM + n] * sx;
-              a.hbuf[static_cast<int64_t>(p) * a.I + 64 * b + r] =
-                  __bfloat16_as_ushort(__float2bfloat16(silu(acc[n] * sx) * up));
-            }
-          }
-        }
-        // orders the h stores before the release below and protects xch
-        named_bar_sync(kBarEpi, 128);
         ++published;
         if (u + 1 == P.ue || (u + 1) / P.per != seg) {
+          // every epilogue thread's stores of this segment before the release
+          named_bar_sync(kBarEpi, 128);
           if (threadIdx.x == kEpi0 * 32) red_release_gpu_add(a.seg_done + seg, published);
           published = 0;
         }
@@ -981,7 +1077,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
   OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
   SlotScales* scales = reinterpret_cast<SlotScales*>(metas + 2);
-  float* xch = reinterpret_cast<float*>(scales + kTSlots);  // [64][kFBM]
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.stages; ++i) {
@@ -1021,7 +1116,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   if (warp < kDQ) {
     dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, scales, deadline);
   } else if (warp < kEpi0 + 4) {
-    epilogue_warps<SK, G>(a, cb, table, metas, scales, xch, deadline);
+    epilogue_warps<SK, G>(a, cb, table, metas, scales, deadline);
   } else if (warp == kMmaWarp) {
     if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, deadline);
     __syncwarp();
@@ -1102,10 +1197,11 @@ static FusedGeometry fused_geometry(int H, int I, int G) {
   f.sk = stage_k(H, I);
   const int gps = f.sk / G;
   f.stage_bytes = round128(static_cast<uint64_t>(f.sk) * 64 + gps * 256 + gps * 64);
-  const int maxrow = H > I ? H : I;
-  f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (2ull * maxrow + 16));
+  // operand rows: bf16 x (2H bytes) or fp32 gate|up (8I bytes)
+  const uint64_t maxrow = 2ull * H > 8ull * I ? 2ull * H : 8ull * I;
+  f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (maxrow + 16));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
-                       kTSlots * sizeof(SlotScales) + 64 * kFBM * sizeof(float);
+                       kTSlots * sizeof(SlotScales);
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;

@@ -10,7 +10,7 @@
 // array compiled into the library instead.
 //
 // The scratch is a file-scope __device__ array of kNoAllocScratchBytes
-// (5 MiB, enough for M <= 48 tokens at H = 2048, I = 512, E = 256, top-8);
+// (6 MiB, enough for M <= 48 tokens at H = 2048, I = 512, E = 256, top-8);
 // every GPU that loads the library holds it until the process exits. Larger
 // requests are rejected with MTP_ERR_WORKSPACE before anything is launched.
 //

@@ -76,7 +76,7 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device, layer):
     from mtp_b200.synthetic import CONFIG1, make_inputs
     lib = _lib.load()
     w, s = layer
-    m = 256  # needs ~21 MB of scratch, far above the 5 MiB array
+    m = 256  # needs ~21 MB of scratch, far above the 6 MiB array
     x, logits = make_inputs(CONFIG1, m, seed=9, device=cuda_device)
     out = torch.zeros((m, CONFIG1.hidden), dtype=torch.bfloat16, device=cuda_device)
     args = _args(x, logits, w, s, out)
