@@ -205,6 +205,29 @@ MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
 #define MTP_NOALLOC_SCRATCH_BYTES (6u << 20)
 MTP_API int mtp_w4a16_moe_layer_noalloc(const MtpMoeLayerArgs* args, void* stream);
 
+
+/* ---- MTP expert-demand predictor (prefetch driver) --------------------------
+ * logits = W2 . silu(W1 . h + b1) + b2 for each hidden state h [M, hidden]
+ * bf16: hidden -> width -> future x experts, then the top_k experts of every
+ * future layer (descending logit, exact ties to the lower expert id) into
+ * ids_out [M, future, top_k] int32. The first layer's activation is rounded to
+ * bf16 before the second linear. Replaces the forward of the reference's
+ * predictor family (training/hidden_residual.py:44-134
+ * HiddenResidualExpertPredictor; training/predictor.py:193-241) and the
+ * topk(logits.float()) ranking of recall_at_m (training/predictor.py:105).
+ * Weights W1 [width, hidden] and W2 [future*experts, width] (bf16, out x in)
+ * are prepacked once by mtp_predictor_pack into the kernel's fragment order
+ * (same byte size). b1 [width] and b2 [future*experts] bf16 may be NULL.
+ * hidden, width: multiples of 128, <= 2048; experts <= 1024; top_k <= 32.   */
+MTP_API int mtp_predictor_pack(const uint16_t* w, int32_t rows, int32_t cols, uint16_t* out, void* stream);
+MTP_API int mtp_predictor_workspace_size(int32_t M, int32_t width, int32_t future, int32_t experts,
+                                         int64_t* bytes);
+MTP_API int mtp_predict_topk(const uint16_t* h, int32_t M, int32_t hidden, const uint16_t* w1_packed,
+                             const uint16_t* b1, int32_t width, const uint16_t* w2_packed,
+                             const uint16_t* b2, int32_t future, int32_t experts, int32_t top_k,
+                             float* logits_out, int32_t* ids_out, void* workspace,
+                             int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,7 @@ interfaces. There is no CPU fallback.
 """
 from ._lib import MtpError, load as load_library  # noqa: F401
 from .ops import (  # noqa: F401
+    MtpPredictor,
     SharedExpert,
     W4A16Experts,
     dequantize_gptq_projection,
@@ -19,6 +20,7 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "MtpError",
+    "MtpPredictor",
     "load_library",
     "SharedExpert",
     "W4A16Experts",

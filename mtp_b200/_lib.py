@@ -27,6 +27,9 @@ EXPORTS = (
     "mtp_w4a16_moe_layer_workspace_size",
     "mtp_w4a16_moe_layer",
     "mtp_w4a16_moe_layer_noalloc",
+    "mtp_predictor_pack",
+    "mtp_predictor_workspace_size",
+    "mtp_predict_topk",
 )
 
 MTP_ZERO_RAW = 0
@@ -67,6 +70,9 @@ _SIGS = {
     "mtp_w4a16_moe_layer_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_w4a16_moe_layer": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
     "mtp_w4a16_moe_layer_noalloc": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
+    "mtp_predictor_pack": (C.c_int, [vp, i32, i32, vp, vp]),
+    "mtp_predictor_workspace_size": (C.c_int, [i32, i32, i32, i32, C.POINTER(i64)]),
+    "mtp_predict_topk": (C.c_int, [vp, i32, i32, vp, vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, i64, vp]),
 }
 
 _lock = threading.Lock()
@@ -129,3 +135,9 @@ def host_device_pointer(host_ptr: int) -> int:
     out = vp()
     call("mtp_host_device_pointer", vp(host_ptr), C.byref(out))
     return int(out.value)
+
+
+def predictor_workspace_bytes(m: int, width: int, future: int, experts: int) -> int:
+    out = i64()
+    call("mtp_predictor_workspace_size", m, width, future, experts, C.byref(out))
+    return out.value

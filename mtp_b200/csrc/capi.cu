@@ -251,4 +251,46 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   return launch_moe_fused(f, st);
 }
 
+
+// ---- MTP expert-demand predictor ----------------------------------------------
+int mtp_predictor_pack(const uint16_t* w, int32_t rows, int32_t cols, uint16_t* out, void* stream) {
+  if (!w || !out) return MTP_ERR_NULL;
+  if (rows <= 0 || cols <= 0 || rows % 16 || cols % 16) return MTP_ERR_SHAPE;
+  if (!aligned(w, 4) || !aligned(out, 16)) return MTP_ERR_ALIGN;
+  return predictor_pack(w, rows, cols, out, static_cast<cudaStream_t>(stream));
+}
+
+static bool predictor_shapes_ok(int M, int hidden, int width, int future, int experts, int k) {
+  if (M < 1 || future < 1 || experts < 1 || experts > 1024 || k < 1 || k > 32 || k > experts) return false;
+  if (hidden < 128 || hidden > 2048 || hidden % 128) return false;
+  if (width < 128 || width > 2048 || width % 128) return false;
+  return (static_cast<int64_t>(future) * experts) % 16 == 0;
+}
+
+int mtp_predictor_workspace_size(int32_t M, int32_t width, int32_t future, int32_t experts, int64_t* bytes) {
+  if (!bytes) return MTP_ERR_NULL;
+  if (M < 1 || width < 1 || future < 1 || experts < 1) return MTP_ERR_SHAPE;
+  *bytes = round_up(2LL * M * width, 256) + round_up(4LL * M * future * experts, 256);
+  return MTP_OK;
+}
+
+int mtp_predict_topk(const uint16_t* h, int32_t M, int32_t hidden, const uint16_t* w1_packed, const uint16_t* b1,
+                     int32_t width, const uint16_t* w2_packed, const uint16_t* b2, int32_t future, int32_t experts,
+                     int32_t top_k, float* logits_out, int32_t* ids_out, void* workspace, int64_t workspace_bytes,
+                     void* stream) {
+  if (!h || !w1_packed || !w2_packed || !ids_out || !workspace) return MTP_ERR_NULL;
+  if (!predictor_shapes_ok(M, hidden, width, future, experts, top_k)) return MTP_ERR_SHAPE;
+  if (!aligned(h, 16) || !aligned(w1_packed, 16) || !aligned(w2_packed, 16) || !aligned(workspace, 256) ||
+      (logits_out && !aligned(logits_out, 4)))
+    return MTP_ERR_ALIGN;
+  int64_t need = 0;
+  mtp_predictor_workspace_size(M, width, future, experts, &need);
+  if (workspace_bytes < need) return MTP_ERR_WORKSPACE;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  uint16_t* hidden2 = reinterpret_cast<uint16_t*>(ws);
+  float* logits = logits_out ? logits_out : reinterpret_cast<float*>(ws + round_up(2LL * M * width, 256));
+  return predictor_run(h, M, hidden, w1_packed, b1, width, w2_packed, b2, future, experts, top_k, logits, ids_out,
+                       hidden2, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

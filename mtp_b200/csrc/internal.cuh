@@ -61,6 +61,11 @@ int repack_gptq(const int32_t* w13q, const int32_t* w13z, const uint16_t* w13s, 
 int gptq_dequant(const int32_t* q, const int32_t* z, const uint16_t* s, const int32_t* gidx, int K,
                  int N, int G, int zero_mode, float* out, cudaStream_t st);
 
+int predictor_pack(const uint16_t* w, int rows, int cols, uint16_t* out, cudaStream_t st);
+int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const uint16_t* b1, int width,
+                  const uint16_t* w2p, const uint16_t* b2, int F, int E, int k, float* logits, int32_t* ids,
+                  uint16_t* hidden2, cudaStream_t st);
+
 bool fused_supported(int H, int I, int G);
 int fused_max_work_segments(int M, int max_seg, int max_blocks);
 int launch_moe_fused(const FusedArgs& a, cudaStream_t st);

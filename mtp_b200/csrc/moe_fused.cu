@@ -1137,9 +1137,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   // The per-call counters are no longer read by anyone: zero them for the
   // next call, a slice per CTA.
   {
-    const int G = gridDim.x, c = blockIdx.x;
-    for (int i = a.E * c / G + threadIdx.x; i < a.E * (c + 1) / G; i += kThreads) a.cnt[i] = 0;
-    for (int i = cb.S * c / G + threadIdx.x; i < cb.S * (c + 1) / G; i += kThreads) a.seg_done[i] = 0;
+    const int nc = gridDim.x, c = blockIdx.x;
+    for (int i = a.E * c / nc + threadIdx.x; i < a.E * (c + 1) / nc; i += kThreads) a.cnt[i] = 0;
+    for (int i = cb.S * c / nc + threadIdx.x; i < cb.S * (c + 1) / nc; i += kThreads) a.seg_done[i] = 0;
   }
   const int quads = a.H / 4;
   const int64_t total = static_cast<int64_t>(a.M) * quads;

@@ -324,3 +324,54 @@ def fused_experts(hidden_states: torch.Tensor, w1: W4A16Experts, w2=None,
         hidden_states.copy_(out)
         return hidden_states
     return out
+
+
+# ---------------------------------------------------------------------------
+# MTP expert-demand predictor
+# ---------------------------------------------------------------------------
+class MtpPredictor:
+    """BF16 predictor ``logits = W2 . silu(W1 . h + b1) + b2`` (hidden -> width
+    -> future x experts) with per-future-layer top-k, the forward of the
+    reference's predictor family (training/hidden_residual.py:44-134) at the
+    BASELINE shape. Weights are prepacked once for the kernel."""
+
+    def __init__(self, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor, b2: torch.Tensor | None,
+                 *, future: int, experts: int):
+        _check_cuda("w1", w1, torch.bfloat16, 2)
+        _check_cuda("w2", w2, torch.bfloat16, 2)
+        _check_cuda("b1", b1, torch.bfloat16, 1)
+        _check_cuda("b2", b2, torch.bfloat16, 1)
+        width, hidden = w1.shape
+        if w2.shape != (future * experts, width):
+            raise ValueError(f"w2 must be [{future * experts}, {width}], got {tuple(w2.shape)}")
+        if b1 is not None and b1.numel() != width:
+            raise ValueError("b1 must have width entries")
+        if b2 is not None and b2.numel() != future * experts:
+            raise ValueError("b2 must have future * experts entries")
+        self.hidden, self.width, self.future, self.experts = hidden, width, future, experts
+        self.w1p = torch.empty_like(w1)
+        self.w2p = torch.empty_like(w2)
+        _lib.call("mtp_predictor_pack", _p(w1), width, hidden, _p(self.w1p), _stream(w1))
+        _lib.call("mtp_predictor_pack", _p(w2), future * experts, width, _p(self.w2p), _stream(w2))
+        self.b1, self.b2 = b1, b2
+
+    def workspace(self, m: int, device) -> torch.Tensor:
+        return torch.empty(_lib.predictor_workspace_bytes(m, self.width, self.future, self.experts),
+                           dtype=torch.uint8, device=device)
+
+    def predict_topk(self, hidden: torch.Tensor, top_k: int, *, logits_out: torch.Tensor | None = None,
+                     ids_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """ids [M, future, top_k] int32 of the predicted experts per future layer."""
+        _check_cuda("hidden", hidden, torch.bfloat16, 2)
+        m = hidden.shape[0]
+        if hidden.shape[1] != self.hidden:
+            raise ValueError(f"hidden must be [M, {self.hidden}]")
+        ids = ids_out if ids_out is not None else torch.empty(m, self.future, top_k, dtype=torch.int32,
+                                                              device=hidden.device)
+        _check_cuda("ids_out", ids, torch.int32)
+        _check_cuda("logits_out", logits_out, torch.float32)
+        ws = workspace if workspace is not None else self.workspace(m, hidden.device)
+        _lib.call("mtp_predict_topk", _p(hidden), m, self.hidden, _p(self.w1p), _p(self.b1), self.width,
+                  _p(self.w2p), _p(self.b2), self.future, self.experts, top_k, _p(logits_out), _p(ids),
+                  _p(ws), ws.numel(), _stream(hidden))
+        return ids

@@ -86,3 +86,33 @@ def make_inputs(cfg: LayerConfig, m: int, seed: int = 1, device="cpu"):
     x = torch.randn((m, cfg.hidden), generator=g, device=device).to(torch.bfloat16)
     logits = torch.randn((m, cfg.num_experts), generator=g, device=device, dtype=torch.float32)
     return x, logits
+
+
+# the MTP predictor, hidden 2048 -> 2048 -> 4 future layers x 256 experts.
+@dataclass(frozen=True)
+class PredictorConfig:
+    hidden: int = 2048
+    width: int = 2048
+    future: int = 4
+    experts: int = 256
+    top_k: int = 8
+    tokens: tuple[int, ...] = (1, 8, 64)
+
+
+CONFIG3 = PredictorConfig()
+
+
+def make_predictor(cfg: PredictorConfig, seed: int = 0, device="cpu", bias: bool = True):
+    """W1 [width, hidden], W2 [future*experts, width] bf16 N(0,1)*0.02, biases bf16 N(0,1)*0.02 (or None)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    w1 = (torch.randn(cfg.width, cfg.hidden, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(cfg.future * cfg.experts, cfg.width, generator=g) * 0.02).to(torch.bfloat16)
+    b1 = (torch.randn(cfg.width, generator=g) * 0.02).to(torch.bfloat16) if bias else None
+    b2 = (torch.randn(cfg.future * cfg.experts, generator=g) * 0.02).to(torch.bfloat16) if bias else None
+    mv = lambda t: None if t is None else t.to(device)  # noqa: E731
+    return mv(w1), mv(b1), mv(w2), mv(b2)
+
+
+def make_predictor_inputs(cfg: PredictorConfig, m: int, seed: int = 0, device="cpu") -> torch.Tensor:
+    g = torch.Generator(device="cpu").manual_seed(10_000 + seed)
+    return torch.randn(m, cfg.hidden, generator=g).to(torch.bfloat16).to(device)
