@@ -68,12 +68,17 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
   const int strip = blockIdx.x;
   const int kpw = K / kPWarps;  // K per warp (<= 256): kpw / 16 k-steps
   const int ks0 = warp * (kpw / 16);
-  // this warp's weight fragments, loaded once (16-byte loads, streaming)
+  // Let the next kernel of the chain start streaming its own weights now.
+  pdl_launch_dependents();
+  // this warp's weight fragments, loaded once (16-byte loads, streaming);
+  // they do not depend on the previous kernel, so they are issued before
+  // waiting for it
   uint4 a[kMaxKPerWarp / 16];
   const uint4* src = wp + (static_cast<int64_t>(strip) * (K / 16) + ks0) * 32 + lane;
 #pragma unroll
   for (int i = 0; i < kMaxKPerWarp / 16; ++i)
     if (i < kpw / 16) a[i] = ldg_stream16(src + i * 32);
+  pdl_wait();  // x is the previous kernel's output
   for (int c0 = 0; c0 < M; c0 += kTokChunk) {
     // stage x rows c0..c0+15 (zero rows past M)
     const int vecs = K / 8;
@@ -131,6 +136,7 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
 __global__ void topk_rows_kernel(const float* __restrict__ logits, int rows, int E, int k,
                                  int32_t* __restrict__ ids) {
   extern __shared__ float tv[];  // [warps][E]
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -202,17 +208,35 @@ int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const ui
     configured_dev = dev;
     configured_smem = smem;
   }
-  gemv_kernel<<<width / 16, kPThreads, gemv_smem(H), st>>>(h, M, H, reinterpret_cast<const uint4*>(w1p), b1, width, 0,
-                                                            hidden2, nullptr);
-  int r = launch_status();
-  if (r != MTP_OK) return r;
+  // Programmatic dependent launches: each kernel may start (and stream its
+  // weights) while the previous one finishes; it waits for it before reading
+  // that kernel's output.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kPThreads);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(width / 16);
+  cfg.dynamicSmemBytes = gemv_smem(H);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, h, M, H, reinterpret_cast<const uint4*>(w1p), b1, width, 0, hidden2,
+                         static_cast<float*>(nullptr)) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
   const int R2 = F * E;
-  gemv_kernel<<<R2 / 16, kPThreads, gemv_smem(width), st>>>(hidden2, M, width, reinterpret_cast<const uint4*>(w2p), b2,
-                                                             R2, 1, nullptr, logits);
-  r = launch_status();
-  if (r != MTP_OK) return r;
+  cfg.gridDim = dim3(R2 / 16);
+  cfg.dynamicSmemBytes = gemv_smem(width);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, static_cast<const uint16_t*>(hidden2), M, width,
+                         reinterpret_cast<const uint4*>(w2p), b2, R2, 1, static_cast<uint16_t*>(nullptr), logits) !=
+      cudaSuccess)
+    return MTP_ERR_LAUNCH;
   const int rows = M * F, wpb = 4;
-  topk_rows_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, static_cast<size_t>(wpb) * E * 4, st>>>(logits, rows, E, k, ids);
+  cfg.blockDim = dim3(wpb * 32);
+  cfg.gridDim = dim3((rows + wpb - 1) / wpb);
+  cfg.dynamicSmemBytes = static_cast<size_t>(wpb) * E * 4;
+  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(logits), rows, E, k, ids) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
   return launch_status();
 }
 
