@@ -228,6 +228,64 @@ MTP_API int mtp_predict_topk(const uint16_t* h, int32_t M, int32_t hidden, const
                              float* logits_out, int32_t* ids_out, void* workspace,
                              int64_t workspace_bytes, void* stream);
 
+
+/* ---- expert prefetch session (premap slot cache) ----------------------------
+ * A per-layer HBM slot cache of expert blobs (slots_per_layer of num_experts
+ * resident per layer) filled from a pinned host store by cudaMemcpyAsync on a
+ * session-owned side stream, and the expert -> slot tables the layer reads
+ * (MtpMoeLayerArgs.slot_table / expert_blobs / host_blobs of layer l:
+ * slot_tables + l * num_experts, cache_base + l * slots_per_layer *
+ * expert_bytes, host_store + l * num_experts * expert_bytes).
+ * Replaces the reference's producer session C-ABI
+ * (premap_payload_cache_inprocess_native_producer_stub.hip: session_create_v1
+ * 505, destroy_v1 570, update_v1 800), which moves no bytes, with the
+ * bookkeeping of its cache managers (runtime/cache_manager.py 193-578), one
+ * LRU per layer. The handle is opaque; calls on one session come from one
+ * host thread. simulate = 1 keeps the bookkeeping only (no CUDA calls, copies
+ * complete at once; pointers may be NULL).                                  */
+typedef struct MtpPrefetchConfig {
+  int32_t device;
+  int32_t num_layers;
+  int32_t num_experts;
+  int32_t slots_per_layer;
+  int64_t expert_bytes;            /* mtp_w4a16_expert_layout().bytes          */
+  const uint8_t* host_store;       /* pinned [num_layers][num_experts][bytes]  */
+  uint8_t* cache_base;             /* device [num_layers][slots][bytes]        */
+  int32_t* slot_tables;            /* device [num_layers][num_experts], set to -1 */
+  int32_t simulate;
+} MtpPrefetchConfig;
+
+typedef struct MtpPrefetchStats {  /* CacheManagerSnapshot counters (cache_manager.py:193-205) */
+  int64_t issued_fetch_count;
+  int64_t used_fetch_count;
+  int64_t unused_fetch_count;      /* resident, prefetched, not yet demanded    */
+  int64_t demand_count;
+  int64_t demand_hit_count;
+  int64_t demand_miss_count;
+  int64_t evicted_before_use_count;
+  int64_t ready_late_miss_count;   /* demanded while its copy was in flight     */
+  int64_t inflight_count;
+  int64_t resident_count;
+  int64_t bytes_copied;
+} MtpPrefetchStats;
+
+MTP_API int mtp_prefetch_session_create(const MtpPrefetchConfig* cfg, uint64_t* out_handle);
+MTP_API int mtp_prefetch_session_destroy(uint64_t handle);
+/* Predicted experts of `layer` (host array): copy the ones neither resident
+ * nor in flight, evicting least recently used slots.                        */
+MTP_API int mtp_prefetch_issue(uint64_t handle, int32_t layer, const int32_t* experts, int32_t count,
+                               int32_t* out_issued);
+/* Record that the work enqueued on compute_stream so far is the last use of
+ * layer's slots: later copies into that layer wait for it.                  */
+MTP_API int mtp_prefetch_layer_used(uint64_t handle, int32_t layer, void* compute_stream);
+/* Demanded experts of `layer` (host array): hit / miss accounting; a hit
+ * needs the copy complete now. insert_on_miss copies missing experts in.    */
+MTP_API int mtp_prefetch_demand(uint64_t handle, int32_t layer, const int32_t* experts, int32_t count,
+                                int32_t insert_on_miss, int32_t* out_hits);
+/* Non-blocking: retire completed copies and report the counters.           */
+MTP_API int mtp_prefetch_poll(uint64_t handle, MtpPrefetchStats* out);
+MTP_API int mtp_prefetch_sync(uint64_t handle);
+
 #ifdef __cplusplus
 }
 #endif

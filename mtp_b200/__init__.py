@@ -8,6 +8,7 @@ interfaces. There is no CPU fallback.
 from ._lib import MtpError, load as load_library  # noqa: F401
 from .ops import (  # noqa: F401
     MtpPredictor,
+    PrefetchSession,
     SharedExpert,
     W4A16Experts,
     dequantize_gptq_projection,
@@ -21,6 +22,7 @@ from .ops import (  # noqa: F401
 __all__ = [
     "MtpError",
     "MtpPredictor",
+    "PrefetchSession",
     "load_library",
     "SharedExpert",
     "W4A16Experts",

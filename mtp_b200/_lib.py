@@ -30,6 +30,13 @@ EXPORTS = (
     "mtp_predictor_pack",
     "mtp_predictor_workspace_size",
     "mtp_predict_topk",
+    "mtp_prefetch_session_create",
+    "mtp_prefetch_session_destroy",
+    "mtp_prefetch_issue",
+    "mtp_prefetch_layer_used",
+    "mtp_prefetch_demand",
+    "mtp_prefetch_poll",
+    "mtp_prefetch_sync",
 )
 
 MTP_ZERO_RAW = 0
@@ -57,6 +64,21 @@ class MtpMoeLayerArgs(C.Structure):
     ]
 
 
+class MtpPrefetchConfig(C.Structure):
+    _fields_ = [("device", i32), ("num_layers", i32), ("num_experts", i32), ("slots_per_layer", i32),
+                ("expert_bytes", i64), ("host_store", vp), ("cache_base", vp), ("slot_tables", vp),
+                ("simulate", i32)]
+
+
+class MtpPrefetchStats(C.Structure):
+    _fields_ = [(n, i64) for n in (
+        "issued_fetch_count", "used_fetch_count", "unused_fetch_count", "demand_count", "demand_hit_count",
+        "demand_miss_count", "evicted_before_use_count", "ready_late_miss_count", "inflight_count",
+        "resident_count", "bytes_copied")]
+
+
+u64 = C.c_uint64
+
 _SIGS = {
     "mtp_status_string": (C.c_char_p, [C.c_int]),
     "mtp_abi_version": (C.c_int, []),
@@ -73,6 +95,13 @@ _SIGS = {
     "mtp_predictor_pack": (C.c_int, [vp, i32, i32, vp, vp]),
     "mtp_predictor_workspace_size": (C.c_int, [i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_predict_topk": (C.c_int, [vp, i32, i32, vp, vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, i64, vp]),
+    "mtp_prefetch_session_create": (C.c_int, [C.POINTER(MtpPrefetchConfig), C.POINTER(u64)]),
+    "mtp_prefetch_session_destroy": (C.c_int, [u64]),
+    "mtp_prefetch_issue": (C.c_int, [u64, i32, vp, i32, C.POINTER(i32)]),
+    "mtp_prefetch_layer_used": (C.c_int, [u64, i32, vp]),
+    "mtp_prefetch_demand": (C.c_int, [u64, i32, vp, i32, i32, C.POINTER(i32)]),
+    "mtp_prefetch_poll": (C.c_int, [u64, C.POINTER(MtpPrefetchStats)]),
+    "mtp_prefetch_sync": (C.c_int, [u64]),
 }
 
 _lock = threading.Lock()

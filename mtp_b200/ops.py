@@ -375,3 +375,93 @@ class MtpPredictor:
                   _p(self.w2p), _p(self.b2), self.future, self.experts, top_k, _p(logits_out), _p(ids),
                   _p(ws), ws.numel(), _stream(hidden))
         return ids
+
+
+# ---------------------------------------------------------------------------
+# expert prefetch session (premap slot cache)
+# ---------------------------------------------------------------------------
+class PrefetchSession:
+    """Per-layer HBM slot cache filled from a pinned host store on a side
+    stream, with the expert -> slot tables the layer kernel reads. Counters
+    follow the reference's cache managers (runtime/cache_manager.py:193-578).
+
+    ``host_store`` is a pinned uint8 tensor [layers, experts, expert_bytes]
+    (or None with ``simulate=True``, bookkeeping only)."""
+
+    def __init__(self, num_layers: int, num_experts: int, slots_per_layer: int, expert_bytes: int,
+                 host_store: torch.Tensor | None = None, device=None, simulate: bool = False):
+        import numpy as np  # noqa: F401  (host arrays below)
+        self.num_layers, self.num_experts, self.slots = num_layers, num_experts, slots_per_layer
+        self.expert_bytes = expert_bytes
+        self.host_store = host_store
+        if simulate:
+            self.cache = self.slot_tables = None
+            dev_index = 0
+        else:
+            if host_store is None or not host_store.is_pinned():
+                raise ValueError("host_store must be a pinned host tensor")
+            if host_store.numel() != num_layers * num_experts * expert_bytes:
+                raise ValueError("host_store must be [layers, experts, expert_bytes] bytes")
+            device = torch.device(device)
+            dev_index = device.index if device.index is not None else torch.cuda.current_device()
+            # 256-byte aligned slots: expert_bytes is a multiple of 256 (expert layout)
+            self.cache = torch.empty(num_layers * slots_per_layer * expert_bytes, dtype=torch.uint8, device=device)
+            self.slot_tables = torch.empty(num_layers, num_experts, dtype=torch.int32, device=device)
+        cfg = _lib.MtpPrefetchConfig(dev_index, num_layers, num_experts, slots_per_layer, expert_bytes,
+                                     None if simulate else host_store.data_ptr(),
+                                     None if simulate else self.cache.data_ptr(),
+                                     None if simulate else self.slot_tables.data_ptr(), int(simulate))
+        h = _lib.u64()
+        _lib.call("mtp_prefetch_session_create", C.byref(cfg), C.byref(h))
+        self.handle = h.value
+
+    @staticmethod
+    def _ids(experts):
+        import numpy as np
+        a = np.ascontiguousarray(np.asarray(experts, dtype=np.int32).reshape(-1))
+        return a, a.ctypes.data_as(C.c_void_p)
+
+    def issue(self, layer: int, experts) -> int:
+        a, p = self._ids(experts)
+        out = i32_()
+        _lib.call("mtp_prefetch_issue", self.handle, layer, p, a.size, C.byref(out))
+        return out.value
+
+    def demand(self, layer: int, experts, insert_on_miss: bool = True) -> int:
+        a, p = self._ids(experts)
+        out = i32_()
+        _lib.call("mtp_prefetch_demand", self.handle, layer, p, a.size, int(insert_on_miss), C.byref(out))
+        return out.value
+
+    def layer_used(self, layer: int, stream: torch.cuda.Stream | None = None):
+        st = stream if stream is not None else torch.cuda.current_stream()
+        _lib.call("mtp_prefetch_layer_used", self.handle, layer, C.c_void_p(st.cuda_stream))
+
+    def poll(self) -> dict:
+        out = _lib.MtpPrefetchStats()
+        _lib.call("mtp_prefetch_poll", self.handle, C.byref(out))
+        return {name: getattr(out, name) for name, _ in out._fields_}
+
+    def sync(self):
+        _lib.call("mtp_prefetch_sync", self.handle)
+
+    def layer_views(self, layer: int):
+        """(expert_blobs, slot_table, host_blobs) of one layer, for moe_layer_w4a16."""
+        s0 = layer * self.slots * self.expert_bytes
+        e0 = layer * self.num_experts * self.expert_bytes
+        return (self.cache[s0:s0 + self.slots * self.expert_bytes], self.slot_tables[layer],
+                self.host_store.reshape(-1)[e0:e0 + self.num_experts * self.expert_bytes])
+
+    def close(self):
+        if getattr(self, "handle", 0):
+            _lib.call("mtp_prefetch_session_destroy", self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+i32_ = C.c_int32
