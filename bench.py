@@ -306,7 +306,116 @@ def run_gpu(args, rank: int, world: int):
         result["e2e"] = e2e
     if not args.no_predictor:
         result["predictor"] = run_predictor(dev, hbm_gbs)
+    if not args.no_prefetch:
+        result["prefetch"] = run_prefetch(dev, layers[0][0], layers[0][1], cfg, args.prefetch_layers,
+                                          args.prefetch_steps)
     return result
+
+
+def config2_choices(layers: int, steps: int, experts: int = 256, k: int = 8, hot: int = 32,
+                    stay: float = 0.6, zipf_s: float = 1.1, seed: int = 2):
+    """Synthetic config-2 routing: per layer a Zipf(s) popularity over a seeded
+    permutation of the experts; pick j of a token at layer l + 1 comes from the
+    layer's 32 most popular experts with probability `stay` when pick j at
+    layer l did, else from the whole Zipf distribution (distinct picks)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, experts + 1, dtype=np.float64)
+    p_all = ranks ** -zipf_s
+    p_all /= p_all.sum()
+    p_hot = p_all[:hot] / p_all[:hot].sum()
+    perms = [rng.permutation(experts) for _ in range(layers)]
+    out = np.zeros((steps, layers, k), dtype=np.int32)
+    for t in range(steps):
+        was_hot = rng.random(k) < 0.5
+        for l in range(layers):
+            picks, hot_flags = [], []
+            for j in range(k):
+                is_hot = was_hot[j] and rng.random() < stay
+                while True:
+                    r = rng.choice(hot, p=p_hot) if is_hot else rng.choice(experts, p=p_all)
+                    e = int(perms[l][r])
+                    if e not in picks:
+                        break
+                picks.append(e)
+                hot_flags.append(r < hot)
+            out[t, l] = picks
+            was_hot = np.array(hot_flags)
+    return out
+
+
+def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
+    """slot-indirected decode, M = 1, 64 of 256 experts
+    resident per layer, misses read from the pinned host store by the layer
+    kernel and copied into the cache (demand insert); prefetch issue = the
+    previous token's experts of the next layer, one layer ahead (the
+    reference's previous-token transition policy). Hit rate = demand_hit /
+    demand_count (runtime/cache_manager.py:193-263). n_layers < 40 bounds the
+    pinned host store (n_layers x 256 x 1.63 MB); the layers share one set of
+    expert bytes."""
+    import numpy as np
+    import torch
+
+    import mtp_b200
+
+    e_bytes = experts.expert_bytes
+    E = experts.num_experts
+    host = torch.empty((n_layers, E, e_bytes), dtype=torch.uint8).pin_memory()
+    one = experts.blobs.reshape(E, e_bytes).cpu()
+    for l in range(n_layers):
+        host[l].copy_(one)
+    sess = mtp_b200.PrefetchSession(n_layers, E, 64, e_bytes, host, device=dev)
+    choices = config2_choices(n_layers, steps)
+    x = torch.randn(1, cfg.hidden, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(dev)
+    ws = mtp_b200.layer_workspace(1, experts, cfg.top_k, dev)
+    out = torch.empty(1, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    logits_host = torch.zeros(steps, n_layers, E, dtype=torch.float32)
+    for t in range(steps):
+        for l in range(n_layers):
+            logits_host[t, l, choices[t, l]] = 8.0 + torch.arange(cfg.top_k, dtype=torch.float32) * 0.01
+    logits_dev = logits_host.to(dev)
+    views = [sess.layer_views(l) for l in range(n_layers)]
+    stream = torch.cuda.current_stream(dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    warm = 8
+    for t in range(steps):
+        if t == warm:
+            torch.cuda.synchronize()
+            base = sess.poll()
+            status.zero_()
+            e0.record(stream)
+        for l in range(n_layers):
+            sess.demand(l, choices[t, l])
+            cache, table, hst = views[l]
+            mtp_b200.moe_layer_w4a16(x, logits_dev[t, l].reshape(1, E), experts, cfg.top_k, shared=shared,
+                                     slot_table=table, slot_cache=cache, host_store=hst, workspace=ws, out=out,
+                                     status=status)
+            sess.layer_used(l, stream)
+            nl = (l + 1) % n_layers
+            if t > 0:
+                sess.issue(nl, choices[t - 1, nl] if nl > l else choices[t, nl])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sess.sync()
+    st = sess.poll()
+    ms = e0.elapsed_time(e1)
+    d = {k: st[k] - base[k] for k in ("issued_fetch_count", "used_fetch_count", "demand_count", "demand_hit_count",
+                                       "demand_miss_count", "ready_late_miss_count", "bytes_copied")}
+    timed = steps - warm
+    res = {"config": f"config2 slot cache: {n_layers} layers (BASELINE: 40; fewer bound the pinned host store), "
+                     "256 experts, 64 slots/layer, M=1, Zipf(1.1) + layer Markov stay 0.6 in top-32, "
+                     "previous-token next-layer issue, demand insert",
+           "steps_timed": timed, "hit_rate": round(d["demand_hit_count"] / max(1, d["demand_count"]), 4),
+           "late_miss_rate": round(d["ready_late_miss_count"] / max(1, d["demand_count"]), 4),
+           "used_per_issued": round(d["used_fetch_count"] / max(1, d["issued_fetch_count"]), 4),
+           "host_served_experts": int(status[0].item()),
+           "tok_s": round(timed / (ms / 1e3), 1), "ms_per_token": round(ms / timed, 3),
+           "h2d_GBps": round(d["bytes_copied"] / (ms / 1e3) / 1e9, 2), "counters": d,
+           "timing": "CUDA events on the compute stream around the timed steps; includes the host-side "
+                     "bookkeeping and launch of every layer call (eager)"}
+    sess.close()
+    return res
 
 
 def run_predictor(dev, hbm_gbs):
@@ -444,6 +553,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-predictor", action="store_true")
+    ap.add_argument("--no-prefetch", action="store_true")
+    ap.add_argument("--prefetch-layers", type=int, default=8)
+    ap.add_argument("--prefetch-steps", type=int, default=512)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
