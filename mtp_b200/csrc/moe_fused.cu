@@ -80,7 +80,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
 constexpr int kMaxStages = 8;
 constexpr int kTSlots = 4;          // tensor-memory ring slots
-constexpr int kAccs = 4;            // independent accumulators per stage (16 columns each)
+constexpr int kAccs = 2;            // independent accumulators per stage (16 columns each)
 constexpr int kTmemCols = 512;
 constexpr int kCtrlBytes = 1024;
 constexpr int kWsCache = 64;        // work segments cached in shared memory per pass
@@ -121,7 +121,7 @@ static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
 struct OperandMeta {
   float sx[kFBM];                // row scale: x = sx * (256 * hi + lo)
   float amax[kDQ][kFBM];         // per-warp row maxima (scratch)
-  int xsum[kFBM][kMaxGroups];    // per quantisation group: sum of the 16-bit row values
+  int xsum[kMaxGroups][kFBM];    // per quantisation group and row: sum of the 16-bit values
 };
 
 // Per row and group of one stage, handed from the dequant warps to the
@@ -550,6 +550,29 @@ __device__ __forceinline__ uint32_t lds8(uint32_t addr) {
   return v;
 }
 
+// Explicit shared-memory accesses by 32-bit shared address (the role
+// functions receive plain pointers; these keep their hot loads and stores on
+// the shared-memory path).
+__device__ __forceinline__ uint32_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts16(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(static_cast<uint16_t>(v)) : "memory");
+}
+__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u8 [%0], %1;" ::"r"(addr), "h"(static_cast<uint16_t>(v)) : "memory");
+}
+
 __device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
   float4 v;
   asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
@@ -723,7 +746,7 @@ __device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* p
   if (t < kFBM * (K / G)) {
     const int n = t / (K / G), g = t % (K / G);
     const int p = pairs[n];
-    meta.xsum[n][g] = p >= 0 ? __ldcg(a.xsq + static_cast<int64_t>(pair_token(a, p)) * (K / G) + g) : 0;
+    meta.xsum[g][n] = p >= 0 ? __ldcg(a.xsq + static_cast<int64_t>(pair_token(a, p)) * (K / G) + g) : 0;
   }
   if (t < kFBM) {
     const int p = pairs[t];
@@ -795,7 +818,7 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
       int sum = v0 + v1 + v2 + v3;
       sum += __shfl_xor_sync(kFullMask, sum, 1);
       sum += __shfl_xor_sync(kFullMask, sum, 2);
-      if (q == 0) atomicAdd(&meta.xsum[n][(16 * cc) / G], sum);
+      if (q == 0) atomicAdd(&meta.xsum[(16 * cc) / G][n], sum);
     }
   }
   if (t < kFBM) {
@@ -816,6 +839,7 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
   constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
   constexpr uint32_t acols = SK / 4;
+  const uint32_t tmem = cb.tmem;
   int st = 0, ts = 0, xb = 0;
   uint32_t ph = 0, tph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -836,56 +860,66 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
       for (int s = 0; s < nst; ++s) {
         if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && lane == 0) record_timeout(a);
         if (!mbar_wait(smem_u32(&cb.dempty[ts]), tph ^ 1u, deadline) && lane == 0) record_timeout(a);
-        const bool valid = cb.stage_valid[st] != 0;
+        const bool valid = lds32(smem_u32(&cb.stage_valid[st])) != 0;
         const uint8_t* stage = stages + static_cast<size_t>(st) * a.stage_bytes;
         const uint32_t sbase = smem_u32(stage);
-        const uint32_t tcol = cb.tmem + lane_addr + ts * acols;
-        SlotScales& ss = scales[ts];
-#pragma unroll
-        for (int g = 0; g < gps; ++g) ss.q[half][g][r] = 0;
-#pragma unroll
-        for (int cp = 0; cp < my_chunks; cp += 2) {
-          const int c0 = half * my_chunks + cp;
-          uint32_t v[16];
-          uint32_t qsum = 0;  // sum of the 64 int4 values of the two chunks
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            uint4 wv = make_uint4(0u, 0u, 0u, 0u);
-            if (valid) wv = lds128(sbase + ((c0 + cc) * 128 + r) * 16);
-            const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t lo = w4[j] & 0x0F0F0F0Fu, hi = (w4[j] >> 4) & 0x0F0F0F0Fu;
-              v[cc * 8 + 2 * j] = lo;
-              v[cc * 8 + 2 * j + 1] = hi;
-              qsum += ((lo + hi) * 0x01010101u) >> 24;  // byte sums <= 30: no carry
-            }
-          }
-          tmem_st16(tcol + c0 * 8, v);
-          ss.q[half][(c0 * 32) / G][r] += static_cast<uint16_t>(qsum);
-        }
+        const uint32_t tcol = tmem + lane_addr + ts * acols;
+        const uint32_t ss = smem_u32(&scales[ts]);
         if (half == 0) {
-          const uint16_t* sc = reinterpret_cast<const uint16_t*>(stage + SK * 64);
-          const uint8_t* zp = stage + SK * 64 + gps * 256;
+          // the stage's scale and zero point of this row, per group
 #pragma unroll
           for (int g = 0; g < gps; ++g) {
             float s_ = 0.f;
             uint32_t z_ = 8;
             if (valid) {
-              s_ = __half2float(__ushort_as_half(sc[g * 128 + r]));
-              if (a.zero_mode == MTP_ZERO_RAW) z_ = (zp[g * 64 + (r >> 1)] >> (4 * (r & 1))) & 0xF;
+              s_ = __half2float(__ushort_as_half(static_cast<uint16_t>(lds16(sbase + SK * 64 + (g * 128 + r) * 2))));
+              if (a.zero_mode == MTP_ZERO_RAW) z_ = (lds8(sbase + SK * 64 + gps * 256 + g * 64 + (r >> 1)) >> (4 * (r & 1))) & 0xF;
             }
-            ss.s[g][r] = s_;
-            ss.z[g][r] = static_cast<uint8_t>(z_);
+            sts32(ss + offsetof(SlotScales, s) + (g * 128 + r) * 4, __float_as_uint(s_));
+            sts8(ss + offsetof(SlotScales, z) + g * 128 + r, z_);
           }
         }
+        uint32_t qsum[gps];
+#pragma unroll
+        for (int g = 0; g < gps; ++g) qsum[g] = 0;
+        // the stage's words of this thread's row and K half, loaded at once so
+        // the shared-memory stage can go back to the producer before the unpack
+        uint4 wq[my_chunks];
+#pragma unroll
+        for (int c = 0; c < my_chunks; ++c) {
+          wq[c] = make_uint4(0u, 0u, 0u, 0u);
+          if (valid) wq[c] = lds128(sbase + ((half * my_chunks + c) * 128 + r) * 16);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&cb.empty[st]));
+#pragma unroll
+        for (int cp = 0; cp < my_chunks; cp += 2) {
+          const int c0 = half * my_chunks + cp;
+          uint32_t v[16];
+          int qs = 0;  // sum of the 64 int4 values of the two chunks
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const uint32_t w4[4] = {wq[cp + cc].x, wq[cp + cc].y, wq[cp + cc].z, wq[cp + cc].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t lo = w4[j] & 0x0F0F0F0Fu, hi = (w4[j] >> 4) & 0x0F0F0F0Fu;
+              v[cc * 8 + 2 * j] = lo;
+              v[cc * 8 + 2 * j + 1] = hi;
+              qs = __dp4a(static_cast<int>(lo + hi), 0x01010101, qs);  // byte sums <= 30: no carry between bytes
+            }
+          }
+          tmem_st16(tcol + c0 * 8, v);
+#pragma unroll
+          for (int g = 0; g < gps; ++g) qsum[g] += ((c0 * 32) / G == g) ? static_cast<uint32_t>(qs) : 0u;
+        }
+        // this K half's share of each group (0 for groups outside the half)
+#pragma unroll
+        for (int g = 0; g < gps; ++g)
+          sts16(ss + offsetof(SlotScales, q) + ((half * kMaxStageGroups + g) * 128 + r) * 2, qsum[g]);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(smem_u32(&cb.afull[ts]));
-          mbar_arrive(smem_u32(&cb.empty[st]));
-        }
+        if (lane == 0) mbar_arrive(smem_u32(&cb.afull[ts]));
         if (++st == a.stages) {
           st = 0;
           ph ^= 1u;
@@ -913,6 +947,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
   constexpr int chunks = SK / 32;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   constexpr int cpg = G / 32, subs = kAccs / (SK / G);
+  const uint32_t tmem = cb.tmem;
   int ts = 0, xb = 0;
   uint32_t tph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -927,12 +962,12 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
       for (int s = 0; s < nst; ++s) {
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline)) record_timeout(a);
         tc_fence_after();
-        const uint32_t a_t = cb.tmem + ts * acols;
-        const uint32_t d_t = cb.tmem + kTSlots * acols + ts * dcols;
+        const uint32_t a_t = tmem + ts * acols;
+        const uint32_t d_t = tmem + kTSlots * acols + ts * dcols;
         // B: 16 rows = the high plane's 8 rows, then (SBO = 8K bytes on) the low
         // plane's; chunk c of 32 k starts 256 bytes further (start field +16).
-        // Four independent accumulators per stage, issued round robin, so one
-        // MMA's latency hides behind the next three: accumulator d holds the
+        // kAccs independent accumulators per stage, issued round robin, so an
+        // MMA's latency hides behind the next one: accumulator d holds the
         // chunks c of group d / subs with c % cpg = d % subs (mod subs).
         const uint64_t desc0 = smem_desc_kmajor(xbase + s * chunks * 256, 128, 8 * K);
 #pragma unroll
@@ -974,6 +1009,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
   constexpr int gps = SK / G, subs = kAccs / gps;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
+  const uint32_t tmem = cb.tmem;
   int ts = 0, xb = 0;
   uint32_t tph = 0;
   int published = 0;
@@ -994,7 +1030,9 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         // the slot's scales come from the dequant warps through afull
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
-        const uint32_t dt = cb.tmem + lane_addr + kTSlots * acols + ts * dcols;
+        const uint32_t dt = tmem + lane_addr + kTSlots * acols + ts * dcols;
+        const uint32_t ss = smem_u32(&scales[ts]);
+        const uint32_t xs = smem_u32(&meta.xsum[0][0]);
 #pragma unroll
         for (int g = 0; g < gps; ++g) {
           // 256 * D_hi + D_lo' summed over the group's accumulators
@@ -1009,15 +1047,18 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 #pragma unroll
             for (int n = 0; n < kFBM; ++n) tsum[n] += 256 * static_cast<int>(d[n]) + static_cast<int>(d[8 + n]);
           }
-          const SlotScales& ss = scales[ts];
-          const float sc = ss.s[g][r];
-          const int z = ss.z[g][r];
-          const int q128 = 128 * (static_cast<int>(ss.q[0][g][r]) + static_cast<int>(ss.q[1][g][r]));
+          const float sc = ldsf(ss + offsetof(SlotScales, s) + (g * 128 + r) * 4);
+          const int z = static_cast<int>(lds8(ss + offsetof(SlotScales, z) + g * 128 + r));
+          const int q128 = 128 * static_cast<int>(lds16(ss + offsetof(SlotScales, q) + (g * 128 + r) * 2) +
+                                                  lds16(ss + offsetof(SlotScales, q) + ((kMaxStageGroups + g) * 128 + r) * 2));
           const int gg = s * gps + g;
+          const uint4 xa = lds128(xs + gg * kFBM * 4), xb4 = lds128(xs + gg * kFBM * 4 + 16);
+          const int xsv[kFBM] = {static_cast<int>(xa.x), static_cast<int>(xa.y), static_cast<int>(xa.z), static_cast<int>(xa.w),
+                                 static_cast<int>(xb4.x), static_cast<int>(xb4.y), static_cast<int>(xb4.z), static_cast<int>(xb4.w)};
 #pragma unroll
           for (int n = 0; n < kFBM; ++n) {
             // sum_k (q - z) v = 256 D_hi + D_lo' + 128 sum q - z sum v
-            const int v = tsum[n] + q128 - z * meta.xsum[n][gg];
+            const int v = tsum[n] + q128 - z * xsv[n];
             acc[n] = fmaf(static_cast<float>(v), sc, acc[n]);
           }
         }
