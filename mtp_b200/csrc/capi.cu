@@ -31,7 +31,7 @@ static AlignSizes align_sizes(int numel, int E, int BM, int pad) {
 constexpr int kMaxExpertsWs = 1024;
 constexpr int kMaxWorkSegments = 32768;
 struct LayerWs {
-  int64_t bar, cnt, seg_done, tw, tid, lists, gate, xq, xsx, xsq, wseg, status, gu, ybuf, total;
+  int64_t bar, cnt, seg_done, tw, tid, lists, gate, xq, wseg, status, gu, ybuf, total;
   int max_ws;
 };
 
@@ -53,9 +53,7 @@ static LayerWs layer_ws(int M, int E, int k, int H, int I) {
   w.tid = take(4LL * numel);
   w.lists = take(4LL * E * M);
   w.gate = take(4LL * M);
-  w.xq = take(2LL * M * H);
-  w.xsx = take(4LL * M);
-  w.xsq = take(4LL * M * (H / 64));
+  w.xq = take(static_cast<int64_t>(M) * xq_row_bytes(H));
   w.wseg = take(4LL * kWsInts * w.max_ws);
   w.status = take(16);
   w.gu = take(8LL * (numel + M) * I);
@@ -236,8 +234,6 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   f.slot_table = a.slot_table; f.host_blobs = a.host_blobs; f.shared_blob = a.shared_blob;
   f.gate = reinterpret_cast<float*>(ws + w.gate);
   f.xq = reinterpret_cast<uint8_t*>(ws + w.xq);
-  f.xsx = reinterpret_cast<float*>(ws + w.xsx);
-  f.xsq = reinterpret_cast<int32_t*>(ws + w.xsq);
   f.bar = reinterpret_cast<int32_t*>(ws + w.bar);
   f.cnt = reinterpret_cast<int32_t*>(ws + w.cnt);
   f.seg_done = reinterpret_cast<int32_t*>(ws + w.seg_done);

@@ -15,6 +15,13 @@ constexpr int kWsInts = 4 + 8 * kWsBlocks;
 //   [3] flags (bit 0 shared expert, bit 1 blob in host memory),
 //   [4..] pair ids (row of h / y), -1 for padding.
 
+// One quantised x row: H high bytes, H offset low bytes, the per-group sums
+// of the 16-bit values (int32, room for groups of 64), the row scale (fp32)
+// and padding to 16 bytes. The meta travels with the row in one bulk copy.
+__host__ __device__ constexpr uint32_t xq_row_bytes(int H) {
+  return 2u * static_cast<uint32_t>(H) + static_cast<uint32_t>(H) / 16u + 16u;
+}
+
 // Device-side arguments of the fused layer kernel (moe_fused.cu).
 struct FusedArgs {
   int M, H, I, E, k, numel, zero_mode, has_shared, G, renorm, max_ws;
@@ -31,9 +38,7 @@ struct FusedArgs {
   const uint8_t* host_blobs;
   const uint8_t* shared_blob;
   float* gate;               // [M] sigmoid(x . w_g)
-  uint8_t* xq;               // [M][2H] quantised x: H high bytes, H offset low bytes
-  float* xsx;                // [M] row scale of xq
-  int32_t* xsq;              // [M][H/G] group sums of the 16-bit values
+  uint8_t* xq;               // [M][xq_row_bytes(H)] quantised x rows, see xq_row_bytes
   int32_t* bar;              // [2] grid barrier (count, generation)    \ zero before the first
   int32_t* cnt;              // [E] pairs per expert                    |  call; every call
   int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero

@@ -318,8 +318,8 @@ __device__ __forceinline__ void pack_hilo(int v0, int v1, int v2, int v3, uint32
 
 // Quantise one token's x row (one warp, lane holding the 8-element vectors
 // lane + 32 j) to 16-bit integers v = round(x / sx), sx = max|x| / 32767, and
-// store them as a high-byte row then an offset low-byte row (xq[t] = 2H
-// bytes), with sx and the per-group sums of v (xsq[t][H / G]).
+// store them as a high-byte row then an offset low-byte row, followed by the
+// per-group sums of v and sx (one xq_row_bytes(H) row per token).
 __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const uint4 (&xv)[8]) {
   const int lane = threadIdx.x & 31;
   const int nvec = a.H / 8;
@@ -334,7 +334,8 @@ __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const 
   }
   mx = warp_max(mx);
   const float inv = mx > 0.f ? 32767.f / mx : 0.f;
-  uint8_t* row = a.xq + static_cast<int64_t>(t) * 2 * a.H;
+  uint8_t* row = a.xq + static_cast<int64_t>(t) * xq_row_bytes(a.H);
+  int32_t* gsum = reinterpret_cast<int32_t*>(row + 2 * a.H);
   const int lpg = a.G / 8;  // lanes (8-element vectors) per group: 8 or 16
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -358,9 +359,9 @@ __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const 
     }
     // a group is lpg consecutive lanes of one j
     for (int o = 1; o < lpg; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
-    if ((lane & (lpg - 1)) == 0 && lane + 32 * j < nvec) a.xsq[static_cast<int64_t>(t) * (a.H / a.G) + (lane + 32 * j) / lpg] = sum;
+    if ((lane & (lpg - 1)) == 0 && lane + 32 * j < nvec) gsum[(lane + 32 * j) / lpg] = sum;
   }
-  if (lane == 0) a.xsx[t] = mx / 32767.f;
+  if (lane == 0) *reinterpret_cast<float*>(row + 2 * a.H + a.H / 16) = mx / 32767.f;
 }
 
 // Phase 1: route this CTA's tokens, count and list the (token, slot) pairs per
@@ -672,9 +673,11 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
   uint32_t xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
-    // W1: quantised x rows (2H bytes); W2: fp32 gate|up rows (8I bytes)
-    const uint32_t row_bytes = pass == 0 ? 2u * a.H : 8u * a.I;
-    const uint32_t row_stride = row_bytes + 16u;
+    // W1: quantised x rows with their meta; W2: fp32 gate|up rows (8I bytes).
+    // An odd number of 16-byte pieces per row keeps the 8 rows' pieces in
+    // distinct bank groups.
+    const uint32_t row_bytes = pass == 0 ? xq_row_bytes(a.H) : 8u * a.I;
+    const uint32_t row_stride = row_bytes | 16u;
     int waited_seg = -1;
     for (int u = P.ub; u < P.ue; ++u) {
       const int seg = u / P.per;
@@ -706,7 +709,7 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
       __syncwarp();
       if (p >= 0) {
         const uint8_t* src = pass == 0
-                                 ? a.xq + static_cast<int64_t>(pair_token(a, p)) * 2 * a.H
+                                 ? a.xq + static_cast<int64_t>(pair_token(a, p)) * xq_row_bytes(a.H)
                                  : reinterpret_cast<const uint8_t*>(a.gu + static_cast<int64_t>(p) * 2 * a.I);
         bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
       }
@@ -722,7 +725,8 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
 // dequant warps (0-7): operand quantisation and the A tiles in tensor memory
 // ---------------------------------------------------------------------------
 // W1 operand: the 8 token rows arrive already quantised (xq rows: K high
-// bytes then K offset low bytes, see quantize_token); rearrange them in place
+// bytes, K offset low bytes, group sums, scale; see quantize_token); take the
+// meta out, then rearrange them in place
 // into the MMA's B layout, both planes K-major in 8-row x 16-byte core
 // matrices ((n, k) at (k / 16) * 128 + n * 16 + k % 16, high plane at [0, 8K),
 // low plane at [8K, 16K)), and fetch each row's scale and group sums. Thread
@@ -734,24 +738,21 @@ __device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* p
                                                 OperandMeta& meta) {
   const int t = threadIdx.x, K = a.H;
   const int pieces = 2 * (K / 16) * kFBM;  // <= 2048: at most 8 per thread
+  const int stride = static_cast<int>(xq_row_bytes(K) | 16u);
   uint4 v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int pc = t + kDQ * 32 * i;
     if (pc < pieces) {
       const int n = pc & 7, cc = pc >> 3;  // cc over both planes: plane = cc / (K / 16)
-      v[i] = *reinterpret_cast<const uint4*>(rows + n * (2 * K + 16) + cc * 16);
+      v[i] = *reinterpret_cast<const uint4*>(rows + n * stride + cc * 16);
     }
   }
   if (t < kFBM * (K / G)) {
     const int n = t / (K / G), g = t % (K / G);
-    const int p = pairs[n];
-    meta.xsum[g][n] = p >= 0 ? __ldcg(a.xsq + static_cast<int64_t>(pair_token(a, p)) * (K / G) + g) : 0;
+    meta.xsum[g][n] = pairs[n] >= 0 ? *reinterpret_cast<const int32_t*>(rows + n * stride + 2 * K + 4 * g) : 0;
   }
-  if (t < kFBM) {
-    const int p = pairs[t];
-    meta.sx[t] = p >= 0 ? __ldcg(a.xsx + pair_token(a, p)) : 0.f;
-  }
+  if (t < kFBM) meta.sx[t] = pairs[t] >= 0 ? *reinterpret_cast<const float*>(rows + t * stride + 2 * K + K / 16) : 0.f;
   named_bar_sync(kBarDequant, kDQ * 32);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -1230,17 +1231,20 @@ struct FusedGeometry {
 
 static uint32_t round128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
 
-// K per stage: 256 when it divides both H and I, else 128.
-static int stage_k(int H, int I) { return (H % 256 == 0 && I % 256 == 0) ? 256 : 128; }
+// K per stage: 256 when it divides both H and I and its groups fit the
+// kAccs accumulators of a stage (G = 128), else 128.
+static int stage_k(int H, int I, int G) {
+  return (H % 256 == 0 && I % 256 == 0 && 256 / G <= kAccs) ? 256 : 128;
+}
 
 static FusedGeometry fused_geometry(int H, int I, int G) {
   FusedGeometry f;
-  f.sk = stage_k(H, I);
+  f.sk = stage_k(H, I, G);
   const int gps = f.sk / G;
   f.stage_bytes = round128(static_cast<uint64_t>(f.sk) * 64 + gps * 256 + gps * 64);
   // operand rows: bf16 x (2H bytes) or fp32 gate|up (8I bytes)
-  const uint64_t maxrow = 2ull * H > 8ull * I ? 2ull * H : 8ull * I;
-  f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (maxrow + 16));
+  const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I) | 16u;
+  f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (xrow > hrow ? xrow : hrow));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
                        kTSlots * sizeof(SlotScales);
   const size_t budget = 227 * 1024;

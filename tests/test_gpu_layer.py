@@ -188,3 +188,20 @@ def test_fused_experts_matches_layer(cuda_device, config1):
     assert torch.equal(a, b)
     with pytest.raises(ValueError):
         mtp_b200.fused_experts(x, w, None, tw, ti, activation="gelu")
+
+
+@pytest.mark.parametrize("h,i,gs", [(512, 256, 64), (2048, 512, 64), (1024, 384, 128), (256, 128, 64)])
+def test_shapes_and_group_sizes_match_oracle(cuda_device, h, i, gs):
+    """Other hidden / intermediate sizes and group 64 (K per stage 128), with
+    random zero points, through the kernel router and with a shared expert."""
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    cfg = LayerConfig(num_experts=32, hidden=h, inter=i, shared=True, group_size=gs, tokens=(24,))
+    experts, shared = make_layer(cfg, seed=h + i + gs, random_zeros=True)
+    w, s = build(experts, shared, cuda_device, gs=gs)
+    x, logits = make_inputs(cfg, 24, seed=5)
+    out = mtp_b200.moe_layer_w4a16(x.to(cuda_device), logits.to(cuda_device), w, 8, shared=s)
+    ow, oids, _ = orouter.topk_softmax(logits.numpy(), 8, True)
+    o = olayer.MoeLayerOracle(experts, shared, group_size=gs)
+    ref = o.moe_tokens(x.float(), torch.as_tensor(oids), torch.as_tensor(ow))
+    check(out, ref)
