@@ -127,7 +127,10 @@ __device__ __forceinline__ float bf16_bits_to_float(uint16_t v) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 // x * sigmoid(x) with a fast reciprocal (-> 0 for very negative x)
-__device__ __forceinline__ float silu_fast(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
+// x * sigmoid(x) with the fast exponential and division (a few ulp in fp32;
+// the result is rounded to bf16 by its callers). For x < -87, exp(-x) is inf
+// and the quotient is -0.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Warp reductions
 __device__ __forceinline__ float warp_sum(float v) {
@@ -199,6 +202,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
     if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() > deadline) return false;
   }
+}
+
+// L2 policy for data read once (the streamed expert weights): evict first,
+// so a pass over more bytes than L2 holds does not push out the data and code
+// that the kernel reuses.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s (below) with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
 }
 
 // 1-D bulk copy global -> shared completing on an mbarrier (no tensor map, no

@@ -607,6 +607,7 @@ __device__ __forceinline__ void stage_pieces(const FusedArgs& a, int pass, int b
 __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages,
                                 uint64_t deadline) {
   const int lane = threadIdx.x & 31;
+  const uint64_t policy = l2_evict_first_policy();
   int st = 0;
   uint32_t ph = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -627,7 +628,8 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
         if (blob != nullptr && !host) {
           if (lane == 0) {
             mbar_arrive_expect_tx(full, pc[0].bytes + pc[1].bytes + pc[2].bytes);
-            for (int i = 0; i < 3; ++i) bulk_g2s(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full);
+            for (int i = 0; i < 3; ++i)
+              bulk_g2s_hint(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full, policy);
           }
         } else {
           // Pinned host memory (demand fetch over the host link): a warp copy
@@ -1112,6 +1114,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
+  static_assert(SK / G >= 1 && SK / G <= kAccs && kAccs % (SK / G) == 0, "a stage's groups share the accumulators");
   extern __shared__ __align__(128) uint8_t smem[];
   Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
   int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
@@ -1309,7 +1312,6 @@ int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {
   a.xbuf_bytes = f.xbuf_bytes;
   a.sk = f.sk;
   if (f.sk == 256 && a.G == 128) return launch_fused_t<256, 128>(a, f, st);
-  if (f.sk == 256 && a.G == 64) return launch_fused_t<256, 64>(a, f, st);
   if (f.sk == 128 && a.G == 128) return launch_fused_t<128, 128>(a, f, st);
   if (f.sk == 128 && a.G == 64) return launch_fused_t<128, 64>(a, f, st);
   return MTP_ERR_SHAPE;
