@@ -56,7 +56,7 @@ static LayerWs layer_ws(int M, int E, int k, int H, int I) {
   w.xq = take(static_cast<int64_t>(M) * xq_row_bytes(H));
   w.wseg = take(4LL * kWsInts * w.max_ws);
   w.status = take(16);
-  w.gu = take(8LL * (numel + M) * I);
+  w.gu = take((numel + M) * (8LL * I + 16));
   w.ybuf = take(4LL * (numel + M) * H);
   w.total = o;
   return w;

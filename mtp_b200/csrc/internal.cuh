@@ -43,7 +43,7 @@ struct FusedArgs {
   int32_t* cnt;              // [E] pairs per expert                    |  call; every call
   int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero
   int32_t* lists;            // [E][M] pair ids per expert
-  float* gu;                 // [numel + M][2I] fp32 W1 sums per pair: gate | up
+  float* gu;                 // [numel + M][2I + 4] fp32 W1 sums per pair: gate | up, combine weight
   float* ybuf;
   uint16_t* out;
   float* out_f32;

@@ -154,6 +154,9 @@ __device__ __forceinline__ const uint8_t* ws_blob(const int* e) {
   return reinterpret_cast<const uint8_t*>((hi << 32) | lo);
 }
 
+// floats per gu row: gate | up sums (2I), the combine weight, padding
+__device__ __forceinline__ int64_t gu_stride(const FusedArgs& a) { return 2LL * a.I + 4; }
+
 __device__ __forceinline__ int pair_token(const FusedArgs& a, int p) {
   return p >= a.numel ? p - a.numel : p / a.k;
 }
@@ -379,8 +382,8 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
     const int t = static_cast<int>(t64);
     if (warp < kRouteWarps) {
       int id = -1;
+      float w = 0.f;
       if (a.logits) {
-        float w;
         router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + slot * a.E, &w, &id);
         if (lane < a.k) {
           a.topk_w[t * a.k + lane] = w;
@@ -388,7 +391,10 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
         }
       } else if (lane < a.k) {
         id = a.topk_ids[t * a.k + lane];
+        w = a.topk_w[t * a.k + lane];
       }
+      // the pair's combine weight travels with its gate|up row to the W2 pass
+      if (lane < a.k) a.gu[static_cast<int64_t>(t * a.k + lane) * gu_stride(a) + 2 * a.I] = w;
       if (lane < a.k && id >= 0 && id < a.E) {
         // an expert holds at most one pair per token (distinct ids per token);
         // a repeated id in a caller-given row is dropped and flagged
@@ -427,7 +433,10 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
           }
         }
         part = warp_sum(part);
-        if (lane == 0) a.gate[t] = 1.f / (1.f + expf(-part));
+        if (lane == 0) {
+          a.gate[t] = 1.f / (1.f + expf(-part));
+          a.gu[static_cast<int64_t>(a.numel + t) * gu_stride(a) + 2 * a.I] = 1.f;
+        }
       }
     }
   }
@@ -675,10 +684,11 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
   uint32_t xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
-    // W1: quantised x rows with their meta; W2: fp32 gate|up rows (8I bytes).
+    // W1: quantised x rows with their meta; W2: fp32 gate|up rows with the
+    // pair's combine weight (8I + 16 bytes).
     // An odd number of 16-byte pieces per row keeps the 8 rows' pieces in
     // distinct bank groups.
-    const uint32_t row_bytes = pass == 0 ? xq_row_bytes(a.H) : 8u * a.I;
+    const uint32_t row_bytes = pass == 0 ? xq_row_bytes(a.H) : 8u * a.I + 16u;
     const uint32_t row_stride = row_bytes | 16u;
     int waited_seg = -1;
     for (int u = P.ub; u < P.ue; ++u) {
@@ -712,7 +722,7 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
       if (p >= 0) {
         const uint8_t* src = pass == 0
                                  ? a.xq + static_cast<int64_t>(pair_token(a, p)) * xq_row_bytes(a.H)
-                                 : reinterpret_cast<const uint8_t*>(a.gu + static_cast<int64_t>(p) * 2 * a.I);
+                                 : reinterpret_cast<const uint8_t*>(a.gu + static_cast<int64_t>(p) * gu_stride(a));
         bulk_g2s(smem_u32(xbufs + xb * a.xbuf_bytes + lane * row_stride), src, row_bytes, xfull);
       }
       if (++xb == 2) {
@@ -769,10 +779,11 @@ __device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* p
   named_bar_sync(kBarDequant, kDQ * 32);
 }
 
-// W2 operand: the 8 pair rows arrive as fp32 W1 sums (K gate values, then K up
-// values); form h = bf16(silu(gate) * up) and quantise it in place to 16-bit
-// integers v = 256 * hi + lo' + 128, laid out as the B planes above, with one
-// scale per row and per-group sums of v. Thread (warp w, lane = 4n + q) owns
+// W2 operand: the 8 pair rows arrive as fp32 W1 sums (K gate values, K up
+// values, the combine weight, padding); form h = bf16(silu(gate) * up) and
+// quantise it in place to 16-bit integers v = 256 * hi + lo' + 128, laid out
+// as the B planes above, with one scale per row (times the combine weight)
+// and per-group sums of v. Thread (warp w, lane = 4n + q) owns
 // the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i.
 template <int G>
 __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta, int K) {
@@ -800,6 +811,10 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
   mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 2));
   if (q == 0) meta.amax[w][n] = mx;
   for (int i = t; i < kFBM * kMaxGroups; i += kDQ * 32) (&meta.xsum[0][0])[i] = 0;
+  // the pair's combine weight (top-k weight, 1 for the shared expert) rides in
+  // the row tail; read before the planes overwrite it, folded into the scale
+  float cw = 0.f;
+  if (t < kFBM) cw = *reinterpret_cast<const float*>(rows + t * (8 * K + 16) + 8 * K);
   named_bar_sync(kBarDequant, kDQ * 32);
   float amax = 0.f;
 #pragma unroll
@@ -827,7 +842,7 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
   if (t < kFBM) {
     float m = 0.f;
     for (int j = 0; j < kDQ; ++j) m = fmaxf(m, meta.amax[j][t]);
-    meta.sx[t] = m / 32767.f;
+    meta.sx[t] = m / 32767.f * cw;
   }
   fence_proxy_async_shared();  // the plane stores are read by the tensor cores
   named_bar_sync(kBarDequant, kDQ * 32);
@@ -1081,7 +1096,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 #pragma unroll
         for (int n = 0; n < kFBM; ++n) {
           const int p = cols[n];
-          if (p >= 0) a.gu[static_cast<int64_t>(p) * 2 * a.I + row] = acc[n] * meta.sx[n];
+          if (p >= 0) a.gu[static_cast<int64_t>(p) * gu_stride(a) + row] = acc[n] * meta.sx[n];
         }
         ++published;
         if (u + 1 == P.ue || (u + 1) / P.per != seg) {
@@ -1095,8 +1110,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         for (int n = 0; n < kFBM; ++n) {
           const int p = cols[n];
           if (p >= 0) {
-            const float w = (p < a.numel ? __ldcg(a.topk_w + p) : 1.f) * meta.sx[n];
-            a.ybuf[static_cast<int64_t>(p) * a.H + 128 * b + r] = acc[n] * w;
+            a.ybuf[static_cast<int64_t>(p) * a.H + 128 * b + r] = acc[n] * meta.sx[n];
           }
         }
       }
@@ -1246,7 +1260,7 @@ static FusedGeometry fused_geometry(int H, int I, int G) {
   const int gps = f.sk / G;
   f.stage_bytes = round128(static_cast<uint64_t>(f.sk) * 64 + gps * 256 + gps * 64);
   // operand rows: bf16 x (2H bytes) or fp32 gate|up (8I bytes)
-  const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I) | 16u;
+  const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I + 16u) | 16u;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (xrow > hrow ? xrow : hrow));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
                        kTSlots * sizeof(SlotScales);
