@@ -6,6 +6,7 @@ The compute runs in ``lib/libmtp_b200.so`` (hand-written CUDA behind a C ABI,
 interfaces. There is no CPU fallback.
 """
 from ._lib import MtpError, load as load_library  # noqa: F401
+from .ep import ExpertParallelMoE, plan_dispatch  # noqa: F401
 from .ops import (  # noqa: F401
     MtpPredictor,
     PrefetchSession,
@@ -20,6 +21,7 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = [
+    "ExpertParallelMoE",
     "MtpError",
     "MtpPredictor",
     "PrefetchSession",
@@ -31,5 +33,6 @@ __all__ = [
     "layer_workspace",
     "moe_align_block_size",
     "moe_layer_w4a16",
+    "plan_dispatch",
     "topk_softmax",
 ]

@@ -1,0 +1,194 @@
+"""Expert-parallel W4A16 MoE layer for prefill: experts sharded across the
+ranks of a process group, tokens dispatched to the ranks that own their
+experts and the partial outputs combined back, one all-to-all each way.
+
+Rank g owns the experts [g * E / G, (g + 1) * E / G). A token's pairs on
+another rank reach it as local expert ids with every foreign pair marked -1,
+which is the ``expert_map`` convention of the kernels this path replaces
+(vLLM ``fused_moe`` with ``expert_map``; the reference consumes it at
+tracing/vllm_wna16_group_plan.py:87-95, and reads the EP map at
+tracing/vllm_router_trace.py:7661-7689). Each rank routes its own tokens, then
+
+1. dispatch: every token row goes once to each rank that owns at least one of
+   its experts (rows deduplicated per destination), with its k local ids and
+   weights (weight 0 and id -1 for pairs owned elsewhere);
+2. local compute: the fused layer kernel on the received rows, given the
+   ids and weights (no router, no shared expert): each received row becomes
+   the weighted sum over its local experts;
+3. combine: the partial rows go back to their home rank, which adds them in
+   fp32 to its shared-expert output and rounds once to bf16.
+
+The exchange runs on ``torch.distributed`` ``all_to_all_single`` (NCCL over
+NVLink on the GPU, gloo in the CPU tests). Row payloads travel as bf16 bits
+in int32 views (two values per word; H is even), the id / weight lists as one
+int32 tensor. The decode configs do not shard: they run one replica per GPU.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class DispatchPlan:
+    """Send side of one dispatch: rows ordered by destination rank, then token."""
+
+    tokens: torch.Tensor        # [S] int64 source token of each sent row
+    counts: list[int]           # rows per destination rank (sums to S)
+    local_ids: torch.Tensor     # [S, k] int32 destination-local expert id, -1 if owned elsewhere
+    local_weights: torch.Tensor  # [S, k] fp32 routing weight, 0 where the id is -1
+
+
+def experts_per_rank(num_experts: int, world: int) -> int:
+    if world < 1 or num_experts % world:
+        raise ValueError(f"{num_experts} experts do not shard evenly over {world} ranks")
+    return num_experts // world
+
+
+def plan_dispatch(topk_ids: torch.Tensor, topk_weights: torch.Tensor, num_experts: int,
+                  world: int) -> DispatchPlan:
+    """Rows to send per destination: token t goes to rank d once when any of
+    its top-k experts lives on d. Ids outside [0, E) are never sent."""
+    if topk_ids.shape != topk_weights.shape or topk_ids.dim() != 2:
+        raise ValueError("topk_ids and topk_weights must both be [M, k]")
+    epr = experts_per_rank(num_experts, world)
+    m, k = topk_ids.shape
+    ids = topk_ids.long()
+    valid = (ids >= 0) & (ids < num_experts)
+    dest = torch.where(valid, ids // epr, torch.full_like(ids, world))   # world = nowhere
+    sends = torch.zeros((m, world + 1), dtype=torch.bool, device=ids.device)
+    sends.scatter_(1, dest, True)
+    sends = sends[:, :world]
+    # (destination, token) pairs in destination-major, token-ascending order
+    pairs = sends.t().nonzero()
+    d_of_row, tokens = pairs[:, 0], pairs[:, 1]
+    counts = torch.bincount(d_of_row, minlength=world).tolist()
+    row_ids = ids[tokens]
+    mine = (dest[tokens] == d_of_row[:, None])
+    local_ids = torch.where(mine, row_ids - d_of_row[:, None] * epr, torch.full_like(row_ids, -1))
+    local_w = torch.where(mine, topk_weights[tokens].float(), torch.zeros_like(topk_weights[tokens].float()))
+    return DispatchPlan(tokens, counts, local_ids.to(torch.int32).contiguous(), local_w.contiguous())
+
+
+def _world(group) -> tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _all_to_all(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int], group,
+                world: int):
+    if world == 1:
+        out.copy_(inp)
+    else:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+
+
+def _exchange_counts(counts: list[int], device, group, world: int) -> list[int]:
+    if world == 1:
+        return list(counts)
+    send = torch.tensor(counts, dtype=torch.int64, device=device)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.tolist()
+
+
+class ExpertParallelMoE:
+    """One expert-parallel MoE layer on this rank.
+
+    ``local_fn(rows, ids, weights)`` computes the received rows: bf16 [R, H],
+    int32 [R, k] local ids (-1 = skip), fp32 [R, k] weights -> bf16 [R, H].
+    ``router_fn(logits, k)`` returns (weights fp32 [M, k], ids int32 [M, k]),
+    ``shared_fn(x)`` the gated shared-expert output bf16 [M, H] (or None).
+    :meth:`for_gpu` wires them to the CUDA kernels; the tests inject CPU
+    versions to check the exchange on gloo ranks. Without an initialised
+    process group the layer runs as a single rank that owns every expert."""
+
+    def __init__(self, num_experts: int, top_k: int, hidden: int, local_fn: Callable,
+                 router_fn: Callable, shared_fn: Callable | None = None, group=None):
+        self.world, self.rank = _world(group)
+        self.num_experts = num_experts
+        self.epr = experts_per_rank(num_experts, self.world)
+        self.top_k = top_k
+        self.hidden = hidden
+        self.local_fn = local_fn
+        self.router_fn = router_fn
+        self.shared_fn = shared_fn
+        self.group = group
+
+    @classmethod
+    def for_gpu(cls, local_experts, num_experts: int, top_k: int, shared=None, renormalize: bool = True,
+                group=None, zero_mode: str = "raw") -> "ExpertParallelMoE":
+        """``local_experts``: this rank's shard (``W4A16Experts.shard``)."""
+        from . import _lib
+        from .ops import layer_workspace, moe_layer_w4a16, topk_softmax
+
+        cache = {}
+
+        def workspace(m, dev):
+            # one zero-filled workspace, grown on demand: every call leaves its
+            # counters zero, so calls of any size up to its own can reuse it
+            need = _lib.layer_workspace_bytes(m, local_experts.num_experts, top_k, local_experts.hidden,
+                                              local_experts.inter)
+            ws = cache.get("ws")
+            if ws is None or ws.numel() < need or ws.device != dev:
+                cache["ws"] = ws = layer_workspace(m, local_experts, top_k, dev)
+            return ws
+
+        def local_fn(rows, ids, weights):
+            return moe_layer_w4a16(rows, None, local_experts, top_k, topk_weights=weights, topk_ids=ids,
+                                   zero_mode=zero_mode, workspace=workspace(rows.shape[0], rows.device))
+
+        def router_fn(logits, k):
+            w, ids, _ = topk_softmax(logits, k, renormalize)
+            return w, ids
+
+        shared_fn = None
+        if shared is not None:
+            def shared_fn(x):
+                m = x.shape[0]
+                none_w = torch.zeros((m, top_k), dtype=torch.float32, device=x.device)
+                none_ids = torch.full((m, top_k), -1, dtype=torch.int32, device=x.device)
+                return moe_layer_w4a16(x, None, local_experts, top_k, shared=shared, topk_weights=none_w,
+                                       topk_ids=none_ids, zero_mode=zero_mode, workspace=workspace(m, x.device))
+
+        return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group)
+
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        """x bf16 [M, H] and router_logits fp32 [M, E] of this rank's tokens -> bf16 [M, H]."""
+        if x.dim() != 2 or x.shape[1] != self.hidden or x.dtype != torch.bfloat16:
+            raise ValueError(f"x must be bf16 [M, {self.hidden}]")
+        if router_logits.shape != (x.shape[0], self.num_experts) or router_logits.dtype != torch.float32:
+            raise ValueError(f"router_logits must be fp32 [M, {self.num_experts}]")
+        m, h, k = x.shape[0], self.hidden, self.top_k
+        dev = x.device
+        weights, ids = self.router_fn(router_logits, k)
+        plan = plan_dispatch(ids, weights, self.num_experts, self.world)
+        recv_counts = _exchange_counts(plan.counts, dev, self.group, self.world)
+        r = sum(recv_counts)
+        # dispatch: token rows (bf16 bits) and the id | weight lists
+        send_rows = x[plan.tokens].view(torch.int32)
+        recv_rows = torch.empty((r, h // 2), dtype=torch.int32, device=dev)
+        _all_to_all(recv_rows, send_rows, recv_counts, plan.counts, self.group, self.world)
+        send_meta = torch.cat([plan.local_ids, plan.local_weights.view(torch.int32)], dim=1)
+        recv_meta = torch.empty((r, 2 * k), dtype=torch.int32, device=dev)
+        _all_to_all(recv_meta, send_meta, recv_counts, plan.counts, self.group, self.world)
+        # local experts on the received rows
+        if r > 0:
+            y = self.local_fn(recv_rows.view(torch.bfloat16), recv_meta[:, :k].contiguous(),
+                              recv_meta[:, k:].contiguous().view(torch.float32))
+        else:
+            y = torch.empty((0, h), dtype=torch.bfloat16, device=dev)
+        # combine: partial rows back to their home rank, summed in fp32
+        back = torch.empty((len(plan.tokens), h // 2), dtype=torch.int32, device=dev)
+        _all_to_all(back, y.contiguous().view(torch.int32), plan.counts, recv_counts, self.group, self.world)
+        acc = torch.zeros((m, h), dtype=torch.float32, device=dev)
+        if self.shared_fn is not None and m > 0:
+            acc += self.shared_fn(x).float()
+        acc.index_add_(0, plan.tokens, back.view(torch.bfloat16).float())
+        return acc.to(torch.bfloat16)
+
+    __call__ = forward

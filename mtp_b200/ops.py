@@ -176,6 +176,15 @@ class W4A16Experts:
                   group_size, _p(blobs), _stream(w13_qweight))
         return cls(blobs, e, hidden, inter, group_size, layout)
 
+    def shard(self, rank: int, world: int) -> "W4A16Experts":
+        """The experts [rank * E / world, (rank + 1) * E / world) as a view: the
+        local expert set of one rank of an expert-parallel group."""
+        if world < 1 or not 0 <= rank < world or self.num_experts % world:
+            raise ValueError(f"{self.num_experts} experts do not shard evenly over {world} ranks")
+        n = self.num_experts // world
+        return W4A16Experts(self.blobs[rank * n:(rank + 1) * n], n, self.hidden, self.inter,
+                            self.group_size, self.layout)
+
 
 @dataclass
 class SharedExpert:
