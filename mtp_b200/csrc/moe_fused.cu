@@ -79,14 +79,23 @@ constexpr int kWarps = 15;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
 constexpr int kMaxStages = 8;
-constexpr int kTSlots = 4;          // tensor-memory ring slots
-constexpr int kAccs = 2;            // independent accumulators per stage (16 columns each)
+constexpr int kMaxTSlots = 4;       // tensor-memory ring slots (at most)
+// Per K-per-stage choices: tensor-memory ring slots (A tile of SK / 4 columns
+// plus the accumulators) and independent accumulators per stage (16 columns
+// each, at least one per quantisation group of the stage).
+template <int SK>
+struct StageCfg {
+  static constexpr int tslots = SK >= 512 ? 2 : 4;
+  static constexpr int accs = SK >= 512 ? 4 : 2;
+};
+__host__ __device__ constexpr int tslots_for(int sk) { return sk >= 512 ? 2 : 4; }
+__host__ __device__ constexpr int accs_for(int sk) { return sk >= 512 ? 4 : 2; }
 constexpr int kTmemCols = 512;
 constexpr int kCtrlBytes = 1024;
 constexpr int kWsCache = 64;        // work segments cached in shared memory per pass
 constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
 constexpr int kMaxGroups = 32;      // K / G for K <= 2048, G >= 64
-constexpr int kMaxStageGroups = 4;  // SK / G for SK <= 256, G >= 64
+constexpr int kMaxStageGroups = 4;  // SK / G: 512 / 128 or 256 / 64 at most
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per layer call
 constexpr int kBarDequant = 1;      // named barrier: the 8 dequant warps
 constexpr int kBarEpi = 2;          // named barrier: the 4 epilogue warps
@@ -103,9 +112,9 @@ struct Ctrl {
   uint64_t xfull[2];            // operand rows landed
   uint64_t xempty[2];           // operand buffer free (MMA commit + 4 epilogue warps)
   uint64_t qfull[2];            // operand quantised (B operand ready)
-  uint64_t afull[kTSlots];      // A tile of a tensor-memory slot written
-  uint64_t dfull[kTSlots];      // accumulators of a slot complete (MMA commit)
-  uint64_t dempty[kTSlots];     // accumulators of a slot read by the epilogue
+  uint64_t afull[kMaxTSlots];   // A tile of a tensor-memory slot written
+  uint64_t dfull[kMaxTSlots];   // accumulators of a slot complete (MMA commit)
+  uint64_t dempty[kMaxTSlots];  // accumulators of a slot read by the epilogue
   uint64_t drain;               // final MMA commit
   int stage_valid[kMaxStages];
   int seg_first[2];   // first work segment of the pass range
@@ -857,6 +866,7 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
   constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
   constexpr uint32_t acols = SK / 4;
+  constexpr int kTS = StageCfg<SK>::tslots;
   const uint32_t tmem = cb.tmem;
   int st = 0, ts = 0, xb = 0;
   uint32_t ph = 0, tph = 0, xph = 0;
@@ -942,7 +952,7 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
           st = 0;
           ph ^= 1u;
         }
-        if (++ts == kTSlots) {
+        if (++ts == kTS) {
           ts = 0;
           tph ^= 1u;
         }
@@ -963,6 +973,7 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
 template <int SK, int G>
 __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs, uint64_t deadline) {
   constexpr int chunks = SK / 32;
+  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   constexpr int cpg = G / 32, subs = kAccs / (SK / G);
   const uint32_t tmem = cb.tmem;
@@ -981,7 +992,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline)) record_timeout(a);
         tc_fence_after();
         const uint32_t a_t = tmem + ts * acols;
-        const uint32_t d_t = tmem + kTSlots * acols + ts * dcols;
+        const uint32_t d_t = tmem + kTS * acols + ts * dcols;
         // B: 16 rows = the high plane's 8 rows, then (SBO = 8K bytes on) the low
         // plane's; chunk c of 32 k starts 256 bytes further (start field +16).
         // kAccs independent accumulators per stage, issued round robin, so an
@@ -997,7 +1008,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
           }
         }
         umma_commit(smem_u32(&cb.dfull[ts]));
-        if (++ts == kTSlots) {
+        if (++ts == kTS) {
           ts = 0;
           tph ^= 1u;
         }
@@ -1025,6 +1036,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
   const int quad = warp & 3;
   const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
+  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
   constexpr int gps = SK / G, subs = kAccs / gps;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   const uint32_t tmem = cb.tmem;
@@ -1048,7 +1060,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         // the slot's scales come from the dequant warps through afull
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
-        const uint32_t dt = tmem + lane_addr + kTSlots * acols + ts * dcols;
+        const uint32_t dt = tmem + lane_addr + kTS * acols + ts * dcols;
         const uint32_t ss = smem_u32(&scales[ts]);
         const uint32_t xs = smem_u32(&meta.xsum[0][0]);
 #pragma unroll
@@ -1083,7 +1095,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&cb.dempty[ts]));
-        if (++ts == kTSlots) {
+        if (++ts == kTS) {
           ts = 0;
           tph ^= 1u;
         }
@@ -1128,7 +1140,10 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
+  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
   static_assert(SK / G >= 1 && SK / G <= kAccs && kAccs % (SK / G) == 0, "a stage's groups share the accumulators");
+  static_assert(SK / G <= kMaxStageGroups && kTS <= kMaxTSlots, "stage groups and slots fit the control blocks");
+  static_assert(kTS * (SK / 4 + kAccs * 16) <= kTmemCols, "tensor-memory ring fits 512 columns");
   extern __shared__ __align__(128) uint8_t smem[];
   Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
   int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
@@ -1147,7 +1162,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
       mbar_init(smem_u32(&cb.xempty[i]), 1 + 4);
       mbar_init(smem_u32(&cb.qfull[i]), 1);
     }
-    for (int i = 0; i < kTSlots; ++i) {
+    for (int i = 0; i < kTS; ++i) {
       mbar_init(smem_u32(&cb.afull[i]), kDQ);
       mbar_init(smem_u32(&cb.dfull[i]), 1);
       mbar_init(smem_u32(&cb.dempty[i]), 4);
@@ -1248,10 +1263,12 @@ struct FusedGeometry {
 
 static uint32_t round128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
 
-// K per stage: 256 when it divides both H and I and its groups fit the
-// kAccs accumulators of a stage (G = 128), else 128.
+// K per stage: the largest of 512, 256, 128 that divides both H and I and
+// whose quantisation groups fit the stage's accumulators.
 static int stage_k(int H, int I, int G) {
-  return (H % 256 == 0 && I % 256 == 0 && 256 / G <= kAccs) ? 256 : 128;
+  for (int sk = 512; sk > 128; sk /= 2)
+    if (H % sk == 0 && I % sk == 0 && sk % G == 0 && sk / G <= accs_for(sk)) return sk;
+  return 128;
 }
 
 static FusedGeometry fused_geometry(int H, int I, int G) {
@@ -1263,7 +1280,7 @@ static FusedGeometry fused_geometry(int H, int I, int G) {
   const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I + 16u) | 16u;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (xrow > hrow ? xrow : hrow));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
-                       kTSlots * sizeof(SlotScales);
+                       tslots_for(f.sk) * sizeof(SlotScales);
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;
@@ -1291,10 +1308,11 @@ bool fused_supported(int H, int I, int G) {
   if (H % 256 || I % 128 || H > 2048 || I > 1024 || H % G || I % G) return false;
   const FusedGeometry f = fused_geometry(H, I, G);
   if (f.sk % G) return false;
-  // tensor memory: kTSlots x (A tile + accumulators) <= 512 columns; every
-  // group of a stage gets a whole number of the kAccs accumulators
-  if (kTSlots * (f.sk / 4 + kAccs * 16) > kTmemCols) return false;
-  if (f.sk / G > kAccs || kAccs % (f.sk / G) || (G / 32) % (kAccs / (f.sk / G))) return false;
+  // tensor memory: slots x (A tile + accumulators) <= 512 columns; every
+  // group of a stage gets a whole number of the stage's accumulators
+  const int ts = tslots_for(f.sk), acc = accs_for(f.sk);
+  if (ts * (f.sk / 4 + acc * 16) > kTmemCols) return false;
+  if (f.sk / G > acc || acc % (f.sk / G) || (G / 32) % (acc / (f.sk / G))) return false;
   return f.stages >= 4;
 }
 
@@ -1325,6 +1343,7 @@ int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {
   a.stage_bytes = f.stage_bytes;
   a.xbuf_bytes = f.xbuf_bytes;
   a.sk = f.sk;
+  if (f.sk == 512 && a.G == 128) return launch_fused_t<512, 128>(a, f, st);
   if (f.sk == 256 && a.G == 128) return launch_fused_t<256, 128>(a, f, st);
   if (f.sk == 128 && a.G == 128) return launch_fused_t<128, 128>(a, f, st);
   if (f.sk == 128 && a.G == 64) return launch_fused_t<128, 64>(a, f, st);
