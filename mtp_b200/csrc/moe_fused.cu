@@ -96,6 +96,8 @@ constexpr int kWsCache = 64;        // work segments cached in shared memory per
 constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
 constexpr int kMaxGroups = 32;      // K / G for K <= 2048, G >= 64
 constexpr int kMaxStageGroups = 4;  // SK / G: 512 / 128 or 256 / 64 at most
+constexpr int kSRing = 8;           // scale ring entries: a stage's group scales and zero points
+constexpr int kSRingBytes = kMaxStageGroups * (256 + 64);
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per layer call
 constexpr int kBarDequant = 1;      // named barrier: the 8 dequant warps
 constexpr int kBarEpi = 2;          // named barrier: the 4 epilogue warps
@@ -116,7 +118,9 @@ struct Ctrl {
   uint64_t dfull[kMaxTSlots];   // accumulators of a slot complete (MMA commit)
   uint64_t dempty[kMaxTSlots];  // accumulators of a slot read by the epilogue
   uint64_t drain;               // final MMA commit
-  int stage_valid[kMaxStages];
+  uint64_t sfull[kSRing];       // scale entry landed (tx count)
+  uint64_t sempty[kSRing];      // scale entry read by the 4 epilogue warps
+  int scale_valid[kSRing];      // 0: the stage's expert has no weights (its terms are zero)
   int seg_first[2];   // first work segment of the pass range
   int cached[2];      // 1 if the pass range's segments are in the table
   int S;              // work segments of this call
@@ -134,12 +138,10 @@ struct OperandMeta {
 };
 
 // Per row and group of one stage, handed from the dequant warps to the
-// epilogue with the tensor-memory slot: scale, zero point, and the sum of the
-// group's int4 values (one partial per K half of the stage).
+// epilogue with the tensor-memory slot: the sum of the group's int4 values
+// (one partial per K half of the stage).
 struct SlotScales {
-  float s[kMaxStageGroups][128];
   uint16_t q[2][kMaxStageGroups][128];
-  uint8_t z[kMaxStageGroups][128];
 };
 
 // Units per work segment: W1 row blocks of 64 gate + 64 up rows, W2 row blocks
@@ -622,12 +624,15 @@ __device__ __forceinline__ void stage_pieces(const FusedArgs& a, int pass, int b
   p[2] = {z0 + grp * 64u, wb + sb, zb};
 }
 
+// Each stage: the int4 words into the weight ring (read and released by the
+// dequant warps), the group scales and zero points into the scale ring (read
+// and released by the epilogue).
 __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages,
-                                uint64_t deadline) {
+                                uint8_t* sring, uint64_t deadline) {
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
-  int st = 0;
-  uint32_t ph = 0;
+  int st = 0, sr = 0;
+  uint32_t ph = 0, sph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int nst = (pass == 0 ? a.H : a.I) / a.sk;
@@ -640,14 +645,20 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
         Piece pc[3];
         stage_pieces(a, pass, b, s, pc);
         if (!mbar_wait(smem_u32(&cb.empty[st]), ph ^ 1u, deadline) && lane == 0) record_timeout(a);
-        uint8_t* dst = stages + static_cast<size_t>(st) * a.stage_bytes;
-        const uint32_t full = smem_u32(&cb.full[st]);
-        if (lane == 0) cb.stage_valid[st] = blob != nullptr;
+        if (!mbar_wait(smem_u32(&cb.sempty[sr]), sph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        uint8_t* dst[3];
+        dst[0] = stages + static_cast<size_t>(st) * a.stage_bytes;
+        dst[1] = sring + sr * kSRingBytes;
+        dst[2] = dst[1] + pc[1].bytes;
+        const uint32_t full = smem_u32(&cb.full[st]), sfull = smem_u32(&cb.sfull[sr]);
+        if (lane == 0) cb.scale_valid[sr] = blob != nullptr;
         if (blob != nullptr && !host) {
           if (lane == 0) {
-            mbar_arrive_expect_tx(full, pc[0].bytes + pc[1].bytes + pc[2].bytes);
-            for (int i = 0; i < 3; ++i)
-              bulk_g2s_hint(smem_u32(dst + pc[i].dst_off), blob + pc[i].src_off, pc[i].bytes, full, policy);
+            mbar_arrive_expect_tx(full, pc[0].bytes);
+            bulk_g2s_hint(smem_u32(dst[0]), blob + pc[0].src_off, pc[0].bytes, full, policy);
+            mbar_arrive_expect_tx(sfull, pc[1].bytes + pc[2].bytes);
+            for (int i = 1; i < 3; ++i)
+              bulk_g2s_hint(smem_u32(dst[i]), blob + pc[i].src_off, pc[i].bytes, sfull, policy);
           }
         } else {
           // Pinned host memory (demand fetch over the host link): a warp copy
@@ -655,7 +666,7 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
           if (blob != nullptr) {
             for (int i = 0; i < 3; ++i) {
               const uint8_t* src = blob + pc[i].src_off;
-              uint8_t* d = dst + pc[i].dst_off;
+              uint8_t* d = dst[i];
               for (uint32_t o = lane * 16u; o < pc[i].bytes; o += 32u * 16u * 8u) {
                 uint4 v[8];
 #pragma unroll
@@ -672,11 +683,18 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
             }
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(full);
+          if (lane == 0) {
+            mbar_arrive(full);
+            mbar_arrive(sfull);
+          }
         }
         if (++st == a.stages) {
           st = 0;
           ph ^= 1u;
+        }
+        if (++sr == kSRing) {
+          sr = 0;
+          sph ^= 1u;
         }
       }
     }
@@ -888,36 +906,19 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
       for (int s = 0; s < nst; ++s) {
         if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && lane == 0) record_timeout(a);
         if (!mbar_wait(smem_u32(&cb.dempty[ts]), tph ^ 1u, deadline) && lane == 0) record_timeout(a);
-        const bool valid = lds32(smem_u32(&cb.stage_valid[st])) != 0;
-        const uint8_t* stage = stages + static_cast<size_t>(st) * a.stage_bytes;
-        const uint32_t sbase = smem_u32(stage);
+        const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
         const uint32_t tcol = tmem + lane_addr + ts * acols;
         const uint32_t ss = smem_u32(&scales[ts]);
-        if (half == 0) {
-          // the stage's scale and zero point of this row, per group
-#pragma unroll
-          for (int g = 0; g < gps; ++g) {
-            float s_ = 0.f;
-            uint32_t z_ = 8;
-            if (valid) {
-              s_ = __half2float(__ushort_as_half(static_cast<uint16_t>(lds16(sbase + SK * 64 + (g * 128 + r) * 2))));
-              if (a.zero_mode == MTP_ZERO_RAW) z_ = (lds8(sbase + SK * 64 + gps * 256 + g * 64 + (r >> 1)) >> (4 * (r & 1))) & 0xF;
-            }
-            sts32(ss + offsetof(SlotScales, s) + (g * 128 + r) * 4, __float_as_uint(s_));
-            sts8(ss + offsetof(SlotScales, z) + g * 128 + r, z_);
-          }
-        }
         uint32_t qsum[gps];
 #pragma unroll
         for (int g = 0; g < gps; ++g) qsum[g] = 0;
         // the stage's words of this thread's row and K half, loaded at once so
-        // the shared-memory stage can go back to the producer before the unpack
+        // the shared-memory stage can go back to the producer before the
+        // unpack (a stage of an expert without weights holds stale words; the
+        // epilogue gives its terms a zero scale)
         uint4 wq[my_chunks];
 #pragma unroll
-        for (int c = 0; c < my_chunks; ++c) {
-          wq[c] = make_uint4(0u, 0u, 0u, 0u);
-          if (valid) wq[c] = lds128(sbase + ((half * my_chunks + c) * 128 + r) * 16);
-        }
+        for (int c = 0; c < my_chunks; ++c) wq[c] = lds128(sbase + ((half * my_chunks + c) * 128 + r) * 16);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&cb.empty[st]));
 #pragma unroll
@@ -1031,7 +1032,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, const OperandMeta* metas,
-                               const SlotScales* scales, uint64_t deadline) {
+                               const SlotScales* scales, const uint8_t* sring, uint64_t deadline) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
@@ -1040,8 +1041,8 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
   constexpr int gps = SK / G, subs = kAccs / gps;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   const uint32_t tmem = cb.tmem;
-  int ts = 0, xb = 0;
-  uint32_t tph = 0;
+  int ts = 0, xb = 0, sr = 0;
+  uint32_t tph = 0, sph = 0;
   int published = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
@@ -1057,12 +1058,30 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
       for (int n = 0; n < kFBM; ++n) acc[n] = 0.f;
       for (int s = 0; s < nst; ++s) {
         if (!mbar_wait(smem_u32(&cb.dfull[ts]), tph, deadline) && lane == 0) record_timeout(a);
-        // the slot's scales come from the dequant warps through afull
+        // the slot's int4 sums come from the dequant warps through afull, the
+        // stage's scales and zero points from the producer through sfull
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline) && lane == 0) record_timeout(a);
+        if (!mbar_wait(smem_u32(&cb.sfull[sr]), sph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
         const uint32_t dt = tmem + lane_addr + kTS * acols + ts * dcols;
         const uint32_t ss = smem_u32(&scales[ts]);
         const uint32_t xs = smem_u32(&meta.xsum[0][0]);
+        const uint32_t se = smem_u32(sring + sr * kSRingBytes);
+        const bool valid = cb.scale_valid[sr] != 0;
+        float scs[gps];
+        int zs[gps];
+#pragma unroll
+        for (int g = 0; g < gps; ++g) {
+          scs[g] = valid ? __half2float(__ushort_as_half(static_cast<uint16_t>(lds16(se + (g * 128 + r) * 2)))) : 0.f;
+          zs[g] = a.zero_mode == MTP_ZERO_RAW ? static_cast<int>((lds8(se + gps * 256 + g * 64 + (r >> 1)) >> (4 * (r & 1))) & 0xF) : 8;
+        }
+        // the scale entry is no longer needed: back to the producer
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&cb.sempty[sr]));
+        if (++sr == kSRing) {
+          sr = 0;
+          sph ^= 1u;
+        }
 #pragma unroll
         for (int g = 0; g < gps; ++g) {
           // 256 * D_hi + D_lo' summed over the group's accumulators
@@ -1077,8 +1096,8 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 #pragma unroll
             for (int n = 0; n < kFBM; ++n) tsum[n] += 256 * static_cast<int>(d[n]) + static_cast<int>(d[8 + n]);
           }
-          const float sc = ldsf(ss + offsetof(SlotScales, s) + (g * 128 + r) * 4);
-          const int z = static_cast<int>(lds8(ss + offsetof(SlotScales, z) + g * 128 + r));
+          const float sc = scs[g];
+          const int z = zs[g];
           const int q128 = 128 * static_cast<int>(lds16(ss + offsetof(SlotScales, q) + (g * 128 + r) * 2) +
                                                   lds16(ss + offsetof(SlotScales, q) + ((kMaxStageGroups + g) * 128 + r) * 2));
           const int gg = s * gps + g;
@@ -1151,6 +1170,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
   OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
   SlotScales* scales = reinterpret_cast<SlotScales*>(metas + 2);
+  uint8_t* sring = reinterpret_cast<uint8_t*>(scales + kTS);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.stages; ++i) {
@@ -1166,6 +1186,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
       mbar_init(smem_u32(&cb.afull[i]), kDQ);
       mbar_init(smem_u32(&cb.dfull[i]), 1);
       mbar_init(smem_u32(&cb.dempty[i]), 4);
+    }
+    for (int i = 0; i < kSRing; ++i) {
+      mbar_init(smem_u32(&cb.sfull[i]), 1);
+      mbar_init(smem_u32(&cb.sempty[i]), 4);
     }
     mbar_init(smem_u32(&cb.drain), 1);
     fence_mbar_init();
@@ -1190,12 +1214,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   if (warp < kDQ) {
     dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, scales, deadline);
   } else if (warp < kEpi0 + 4) {
-    epilogue_warps<SK, G>(a, cb, table, metas, scales, deadline);
+    epilogue_warps<SK, G>(a, cb, table, metas, scales, sring, deadline);
   } else if (warp == kMmaWarp) {
     if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, deadline);
     __syncwarp();
   } else if (warp == kWProd) {
-    weight_producer(a, cb, table, stages, deadline);
+    weight_producer(a, cb, table, stages, sring, deadline);
   } else if (warp == kBProd) {
     operand_producer(a, cb, table, xbufs, deadline);
   }
@@ -1263,30 +1287,36 @@ struct FusedGeometry {
 
 static uint32_t round128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
 
-// K per stage: the largest of 512, 256, 128 that divides both H and I and
-// whose quantisation groups fit the stage's accumulators.
-static int stage_k(int H, int I, int G) {
-  for (int sk = 512; sk > 128; sk /= 2)
-    if (H % sk == 0 && I % sk == 0 && sk % G == 0 && sk / G <= accs_for(sk)) return sk;
-  return 128;
-}
+constexpr int kMinStages = 4;  // weight stages in flight at least
 
-static FusedGeometry fused_geometry(int H, int I, int G) {
+static FusedGeometry geometry_for(int H, int I, int sk) {
   FusedGeometry f;
-  f.sk = stage_k(H, I, G);
-  const int gps = f.sk / G;
-  f.stage_bytes = round128(static_cast<uint64_t>(f.sk) * 64 + gps * 256 + gps * 64);
-  // operand rows: bf16 x (2H bytes) or fp32 gate|up (8I bytes)
+  f.sk = sk;
+  f.stage_bytes = round128(static_cast<uint64_t>(sk) * 64);
+  static_assert(kSRingBytes % 16 == 0, "scale ring entries are bulk-copy destinations");
+  // operand rows: quantised x with its meta, or fp32 gate|up with the combine weight
   const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I + 16u) | 16u;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (xrow > hrow ? xrow : hrow));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
-                       tslots_for(f.sk) * sizeof(SlotScales);
+                       tslots_for(sk) * sizeof(SlotScales) + kSRing * kSRingBytes;
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;
   f.stages = s;
   f.smem = fixed + static_cast<size_t>(s) * f.stage_bytes;
   return f;
+}
+
+// K per stage: the largest of 512, 256, 128 that divides both H and I, whose
+// quantisation groups fit the stage's accumulators and that leaves room for
+// kMinStages stages in shared memory (the operand buffers grow with H and I).
+static FusedGeometry fused_geometry(int H, int I, int G) {
+  for (int sk = 512; sk > 128; sk /= 2) {
+    if (H % sk || I % sk || sk % G || sk / G > accs_for(sk)) continue;
+    const FusedGeometry f = geometry_for(H, I, sk);
+    if (f.stages >= kMinStages) return f;
+  }
+  return geometry_for(H, I, 128);
 }
 
 static int device_sms() {
@@ -1313,7 +1343,7 @@ bool fused_supported(int H, int I, int G) {
   const int ts = tslots_for(f.sk), acc = accs_for(f.sk);
   if (ts * (f.sk / 4 + acc * 16) > kTmemCols) return false;
   if (f.sk / G > acc || acc % (f.sk / G) || (G / 32) % (acc / (f.sk / G))) return false;
-  return f.stages >= 4;
+  return f.stages >= kMinStages;
 }
 
 int fused_max_work_segments(int M, int max_seg, int max_blocks) {

@@ -190,10 +190,13 @@ def test_fused_experts_matches_layer(cuda_device, config1):
         mtp_b200.fused_experts(x, w, None, tw, ti, activation="gelu")
 
 
-@pytest.mark.parametrize("h,i,gs", [(512, 256, 64), (2048, 512, 64), (1024, 384, 128), (256, 128, 64)])
+@pytest.mark.parametrize("h,i,gs", [(512, 256, 64), (2048, 512, 64), (1024, 384, 128), (256, 128, 64),
+                                    (2048, 1024, 128), (2048, 768, 128)])
 def test_shapes_and_group_sizes_match_oracle(cuda_device, h, i, gs):
-    """Other hidden / intermediate sizes and group 64 (K per stage 128), with
-    random zero points, through the kernel router and with a shared expert."""
+    """Other hidden / intermediate sizes and group 64, with random zero points,
+    through the kernel router and with a shared expert: K per stage 512, 256
+    (I = 768) and 128 (group 64; I = 1024, whose operand buffers leave room for
+    four stages of 128 only)."""
     import mtp_b200
     from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
     cfg = LayerConfig(num_experts=32, hidden=h, inter=i, shared=True, group_size=gs, tokens=(24,))
