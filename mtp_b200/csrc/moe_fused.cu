@@ -256,6 +256,76 @@ __device__ __forceinline__ int cta_exclusive_scan(int v, int* total, int* tmp) {
 // id, optional renormalisation with the sum clamped to 1e-20 (vLLM
 // topk_softmax as tracing/vllm_router_trace.py:4201-4227 restates it). Lane
 // j < k returns pick j.
+// Router for one token by one warp with the logits in registers (E <= 256:
+// eight per lane, lane l holding ids l, l + 32, ...). Same selection as
+// router_warp below: softmax over all E, top-k descending, exact ties to the
+// lower expert; the probability is exp(v - max) times 1 / sum.
+__device__ __forceinline__ void router_warp_regs(const float* __restrict__ row, int E, int k, int renorm,
+                                                 float* w_out, int* id_out) {
+  const int lane = threadIdx.x & 31;
+  float x[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = 32 * j + lane;
+    x[j] = i < E ? __ldg(row + i) : -INFINITY;
+  }
+  float mx = x[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) mx = fmaxf(mx, x[j]);
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (32 * j + lane < E) s += expf(x[j] - mx);
+  s = warp_sum(s);
+  const float inv_s = 1.f / s;
+  // each lane's best untaken candidate; `taken` marks the lane's picked slots
+  uint32_t taken = 0;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (32 * j + lane < E && x[j] > bv) {
+      bv = x[j];
+      bi = 32 * j + lane;
+    }
+  float my_w = 0.f, wsum = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < k; ++r) {
+    float wv = bv;
+    int wi = bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kFullMask, wv, o);
+      const int oi = __shfl_xor_sync(kFullMask, wi, o);
+      if (ov > wv || (ov == wv && oi < wi)) {
+        wv = ov;
+        wi = oi;
+      }
+    }
+    const float p = expf(wv - mx) * inv_s;
+    wsum += p;
+    if (lane == r) {
+      my_w = p;
+      my_id = wi;
+    }
+    if (wi < E && (wi & 31) == lane) {  // the winner's lane drops it and rescans its registers
+      taken |= 1u << (wi >> 5);
+      bv = -INFINITY;
+      bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (!((taken >> j) & 1u) && 32 * j + lane < E && x[j] > bv) {
+          bv = x[j];
+          bi = 32 * j + lane;
+        }
+    }
+  }
+  if (renorm) my_w = my_w / fmaxf(wsum, 1e-20f);
+  *w_out = my_w;
+  *id_out = my_id;
+}
+
 __device__ __forceinline__ void router_warp(const float* __restrict__ row, int E, int k, int renorm, float* v,
                                             float* w_out, int* id_out) {
   const int lane = threadIdx.x & 31;
@@ -395,7 +465,10 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
       int id = -1;
       float w = 0.f;
       if (a.logits) {
-        router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + slot * a.E, &w, &id);
+        if (a.E <= 256)
+          router_warp_regs(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, &w, &id);
+        else
+          router_warp(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.k, a.renorm, scratch + slot * a.E, &w, &id);
         if (lane < a.k) {
           a.topk_w[t * a.k + lane] = w;
           a.topk_ids[t * a.k + lane] = id;
@@ -418,18 +491,16 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
       // quantised once for every expert that uses it (see quantize_token), and
       // sigmoid(x . w_g) for the shared expert.
       const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(t) * a.H);
+      const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
       const int nvec = a.H / 8;  // <= 256: at most 8 per lane
-      uint4 xv[8];
+      uint4 xv[8], wv[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 8; ++j) {
         if (lane + 32 * j < nvec) xv[j] = xr[lane + 32 * j];
+        if (a.has_shared && lane + 32 * j < nvec) wv[j] = __ldg(wg + lane + 32 * j);
+      }
       quantize_token(a, t, xv);
       if (a.has_shared) {
-        const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
-        uint4 wv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (lane + 32 * j < nvec) wv[j] = wg[lane + 32 * j];
         float part = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
