@@ -616,22 +616,27 @@ __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scrat
     }
   }
   __syncthreads();
+  // the entries of both passes' ranges at once (their list reads overlap)
+  int first[2], n[2];
+  bool cached[2];
   for (int pass = 0; pass < 2; ++pass) {
     const int upg = units_per_segment(a, pass);
     int ub, ue;
     unit_range(S * upg, ub, ue);
-    const int first = ub / upg;
-    const int last = ue > ub ? (ue - 1) / upg : first - 1;
-    const int n = last - first + 1;
-    const bool cached = n <= kWsCache;
+    first[pass] = ub / upg;
+    const int last = ue > ub ? (ue - 1) / upg : first[pass] - 1;
+    n[pass] = last - first[pass] + 1;
+    cached[pass] = n[pass] <= kWsCache;
     if (tid == 0) {
-      cb.seg_first[pass] = first;
-      cb.cached[pass] = cached;
+      cb.seg_first[pass] = first[pass];
+      cb.cached[pass] = cached[pass];
     }
-    for (int i = tid; i < n; i += nt) {
-      int* w = cached ? table + (pass * kWsCache + i) * kWsInts : a.wseg + static_cast<size_t>(first + i) * kWsInts;
-      fill_entry(a, first + i, shared_ws, cnt, sbase, w);
-    }
+  }
+  for (int i = tid; i < n[0] + n[1]; i += nt) {
+    const int pass = i < n[0] ? 0 : 1, j = i - (pass ? n[0] : 0);
+    int* w = cached[pass] ? table + (pass * kWsCache + j) * kWsInts
+                          : a.wseg + static_cast<size_t>(first[pass] + j) * kWsInts;
+    fill_entry(a, first[pass] + j, shared_ws, cnt, sbase, w);
   }
   __syncthreads();
 }

@@ -208,3 +208,25 @@ def test_shapes_and_group_sizes_match_oracle(cuda_device, h, i, gs):
     o = olayer.MoeLayerOracle(experts, shared, group_size=gs)
     ref = o.moe_tokens(x.float(), torch.as_tensor(oids), torch.as_tensor(ow))
     check(out, ref)
+
+
+@pytest.mark.parametrize("e,k,m", [(512, 6, 12), (64, 1, 9), (128, 4, 33)])
+def test_expert_counts_and_top_k_match_oracle(cuda_device, e, k, m):
+    """Other expert counts and top-k widths through the kernel router: E > 256
+    takes the shared-memory router, E <= 256 the register router; M = 33
+    spans more than one token block of the shared expert."""
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    cfg = LayerConfig(num_experts=e, hidden=512, inter=256, top_k=k, shared=True, tokens=(m,))
+    experts, shared = make_layer(cfg, seed=e + k, random_zeros=True)
+    w, s = build(experts, shared, cuda_device)
+    x, logits = make_inputs(cfg, m, seed=3)
+    tw = torch.empty(m, k, device=cuda_device)
+    ti = torch.empty(m, k, dtype=torch.int32, device=cuda_device)
+    out = mtp_b200.moe_layer_w4a16(x.to(cuda_device), logits.to(cuda_device), w, k, shared=s, topk_out=(tw, ti))
+    ow, oids, _ = orouter.topk_softmax(logits.numpy(), k, True)
+    assert np.array_equal(ti.cpu().numpy(), oids)
+    np.testing.assert_allclose(tw.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+    o = olayer.MoeLayerOracle(experts, shared)
+    ref = o.moe_tokens(x.float(), torch.as_tensor(oids), torch.as_tensor(ow))
+    check(out, ref)
