@@ -205,17 +205,16 @@ __device__ __forceinline__ void record_timeout(const FusedArgs& a) { atomicOr(a.
 // arriver clears the arrival count before it publishes the new generation, so
 // the count is zero again for the next barrier and the next call.
 __device__ __forceinline__ bool grid_sync(const FusedArgs& a, int target, uint64_t deadline) {
-  __threadfence();
-  const int old = atomicAdd(a.bar, 1);
+  // arrival releases this CTA's writes (ordered before it by the CTA barrier)
+  // and, for the last arriver, acquires everyone else's
+  const int old = atom_acq_rel_gpu_add(a.bar, 1);
   if (old == static_cast<int>(gridDim.x) - 1) {
     atomicExch(a.bar, 0);
-    __threadfence();
-    red_release_gpu_add(a.bar + 1, 1);
+    red_release_gpu_add(a.bar + 1, 1);  // ordered after the reset
     return true;
   }
   while (static_cast<int>(static_cast<uint32_t>(ld_acquire_gpu(a.bar + 1)) - static_cast<uint32_t>(target)) < 0) {
     if (global_timer_ns() > deadline) return false;
-    __nanosleep(32);
   }
   return true;
 }
