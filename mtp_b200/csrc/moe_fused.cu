@@ -72,10 +72,12 @@ namespace mtp {
 constexpr int kFBM = 8;             // pairs per token block = MMA N
 constexpr int kDQ = 8;              // dequant warps 0-7
 constexpr int kEpi0 = 8;            // epilogue warps 8-11
-constexpr int kMmaWarp = 12;
+constexpr int kMmaWarp = 12;        // MMA issue: even stages (and the tensor-memory allocation)
 constexpr int kWProd = 13;          // weight producer warp
 constexpr int kBProd = 14;          // operand producer warp
-constexpr int kWarps = 15;
+constexpr int kMmaWarp2 = 15;       // MMA issue: odd stages
+constexpr int kMmaIssuers = 2;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
 constexpr int kMaxStages = 8;
@@ -112,7 +114,7 @@ struct Ctrl {
   uint64_t full[kMaxStages];    // weight stage landed (tx count)
   uint64_t empty[kMaxStages];   // weight stage consumed by the dequant warps
   uint64_t xfull[2];            // operand rows landed
-  uint64_t xempty[2];           // operand buffer free (MMA commit + 4 epilogue warps)
+  uint64_t xempty[2];           // operand buffer free (one commit per MMA issuer + 4 epilogue warps)
   uint64_t qfull[2];            // operand quantised (B operand ready)
   uint64_t afull[kMaxTSlots];   // A tile of a tensor-memory slot written
   uint64_t dfull[kMaxTSlots];   // accumulators of a slot complete (MMA commit)
@@ -632,10 +634,11 @@ __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scrat
     }
   }
   for (int i = tid; i < n[0] + n[1]; i += nt) {
-    const int pass = i < n[0] ? 0 : 1, j = i - (pass ? n[0] : 0);
-    int* w = cached[pass] ? table + (pass * kWsCache + j) * kWsInts
-                          : a.wseg + static_cast<size_t>(first[pass] + j) * kWsInts;
-    fill_entry(a, first[pass] + j, shared_ws, cnt, sbase, w);
+    const bool p1 = i >= n[0];
+    const int j = p1 ? i - n[0] : i, f = p1 ? first[1] : first[0];
+    int* w = (p1 ? cached[1] : cached[0]) ? table + ((p1 ? kWsCache : 0) + j) * kWsInts
+                                          : a.wseg + static_cast<size_t>(f + j) * kWsInts;
+    fill_entry(a, f + j, shared_ws, cnt, sbase, w);
   }
   __syncthreads();
 }
@@ -1046,14 +1049,20 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
 // ---------------------------------------------------------------------------
 // MMA issuer (warp 12, one thread)
 // ---------------------------------------------------------------------------
+// Two issuing threads in warps on different SM sub-partitions take alternate
+// stages: a thread that waits for its next stage's A tile (an mbarrier wait)
+// lets the tensor pipe run dry, so the other thread's stage keeps it busy
+// meanwhile. Both walk every unit (operand waits, slot and buffer counters)
+// and each commits the operand buffer after its own MMAs of a unit.
 template <int SK, int G>
-__device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs, uint64_t deadline) {
+__device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs, int which,
+                           uint64_t deadline) {
   constexpr int chunks = SK / 32;
   constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   constexpr int cpg = G / 32, subs = kAccs / (SK / G);
   const uint32_t tmem = cb.tmem;
-  int ts = 0, xb = 0;
+  int ts = 0, xb = 0, g = 0;
   uint32_t tph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
@@ -1064,7 +1073,14 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
       const bool keep = u + 1 < P.ue && reuses_operand(P, u + 1);
       if (!reuse && !mbar_wait(smem_u32(&cb.qfull[xb]), xph, deadline)) record_timeout(a);
       const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
-      for (int s = 0; s < nst; ++s) {
+      for (int s = 0; s < nst; ++s, ++g) {
+        if ((g & 1) != which) {  // the other issuer's stage
+          if (++ts == kTS) {
+            ts = 0;
+            tph ^= 1u;
+          }
+          continue;
+        }
         if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline)) record_timeout(a);
         tc_fence_after();
         const uint32_t a_t = tmem + ts * acols;
@@ -1254,7 +1270,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&cb.xfull[i]), 1);
-      mbar_init(smem_u32(&cb.xempty[i]), 1 + 4);
+      mbar_init(smem_u32(&cb.xempty[i]), kMmaIssuers + 4);
       mbar_init(smem_u32(&cb.qfull[i]), 1);
     }
     for (int i = 0; i < kTS; ++i) {
@@ -1266,7 +1282,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
       mbar_init(smem_u32(&cb.sfull[i]), 1);
       mbar_init(smem_u32(&cb.sempty[i]), 4);
     }
-    mbar_init(smem_u32(&cb.drain), 1);
+    mbar_init(smem_u32(&cb.drain), kMmaIssuers);
     fence_mbar_init();
     cb.gen0 = ld_acquire_gpu(a.bar + 1);
   }
@@ -1290,8 +1306,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, scales, deadline);
   } else if (warp < kEpi0 + 4) {
     epilogue_warps<SK, G>(a, cb, table, metas, scales, sring, deadline);
-  } else if (warp == kMmaWarp) {
-    if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, deadline);
+  } else if (warp == kMmaWarp || warp == kMmaWarp2) {
+    if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, warp == kMmaWarp2 ? 1 : 0, deadline);
     __syncwarp();
   } else if (warp == kWProd) {
     weight_producer(a, cb, table, stages, sring, deadline);
