@@ -91,6 +91,7 @@ struct StageCfg {
   static constexpr int accs = SK >= 512 ? 4 : 2;
 };
 __host__ __device__ constexpr int tslots_for(int sk) { return sk >= 512 ? 2 : 4; }
+constexpr int kQCols = 4;  // tensor-memory columns per slot for the rows' int4 sums per group
 __host__ __device__ constexpr int accs_for(int sk) { return sk >= 512 ? 4 : 2; }
 constexpr int kTmemCols = 512;
 constexpr int kCtrlBytes = 1024;
@@ -120,7 +121,6 @@ struct Ctrl {
   uint64_t dfull[kMaxTSlots];   // accumulators of a slot complete (MMA commit)
   uint64_t dempty[kMaxTSlots];  // accumulators of a slot read by the epilogue
   uint64_t drain;               // final MMA commit
-  uint64_t sfull[kSRing];       // scale entry landed (tx count)
   uint64_t sempty[kSRing];      // scale entry read by the 4 epilogue warps
   int scale_valid[kSRing];      // 0: the stage's expert has no weights (its terms are zero)
   int seg_first[2];   // first work segment of the pass range
@@ -139,12 +139,6 @@ struct OperandMeta {
   int xsum[kMaxGroups][kFBM];    // per quantisation group and row: sum of the 16-bit values
 };
 
-// Per row and group of one stage, handed from the dequant warps to the
-// epilogue with the tensor-memory slot: the sum of the group's int4 values
-// (one partial per K half of the stage).
-struct SlotScales {
-  uint16_t q[2][kMaxStageGroups][128];
-};
 
 // Units per work segment: W1 row blocks of 64 gate + 64 up rows, W2 row blocks
 // of 128 rows.
@@ -728,15 +722,15 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
         dst[0] = stages + static_cast<size_t>(st) * a.stage_bytes;
         dst[1] = sring + sr * kSRingBytes;
         dst[2] = dst[1] + pc[1].bytes;
-        const uint32_t full = smem_u32(&cb.full[st]), sfull = smem_u32(&cb.sfull[sr]);
+        const uint32_t full = smem_u32(&cb.full[st]);
         if (lane == 0) cb.scale_valid[sr] = blob != nullptr;
         if (blob != nullptr && !host) {
           if (lane == 0) {
-            mbar_arrive_expect_tx(full, pc[0].bytes);
-            bulk_g2s_hint(smem_u32(dst[0]), blob + pc[0].src_off, pc[0].bytes, full, policy);
-            mbar_arrive_expect_tx(sfull, pc[1].bytes + pc[2].bytes);
-            for (int i = 1; i < 3; ++i)
-              bulk_g2s_hint(smem_u32(dst[i]), blob + pc[i].src_off, pc[i].bytes, sfull, policy);
+            // the scales and zero points complete on the weight stage's barrier:
+            // the dequant warps acquire both, the epilogue through the MMA's commit
+            mbar_arrive_expect_tx(full, pc[0].bytes + pc[1].bytes + pc[2].bytes);
+            for (int i = 0; i < 3; ++i)
+              bulk_g2s_hint(smem_u32(dst[i]), blob + pc[i].src_off, pc[i].bytes, full, policy);
           }
         } else {
           // Pinned host memory (demand fetch over the host link): a warp copy
@@ -761,10 +755,7 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
             }
           }
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(full);
-            mbar_arrive(sfull);
-          }
+          if (lane == 0) mbar_arrive(full);
         }
         if (++st == a.stages) {
           st = 0;
@@ -955,14 +946,15 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
 
 template <int SK, int G>
 __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* stages, uint8_t* xbufs,
-                              OperandMeta* metas, SlotScales* scales, uint64_t deadline) {
+                              OperandMeta* metas, uint64_t deadline) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3, half = warp >> 2;
   const int r = 32 * quad + lane;  // weight row = tensor-memory lane
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
   constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
-  constexpr uint32_t acols = SK / 4;
+  constexpr uint32_t acols = SK / 4, dcols = StageCfg<SK>::accs * 16;
   constexpr int kTS = StageCfg<SK>::tslots;
+  static_assert(gps <= kQCols, "a stage's groups fit the sum columns");
   const uint32_t tmem = cb.tmem;
   int st = 0, ts = 0, xb = 0;
   uint32_t ph = 0, tph = 0, xph = 0;
@@ -986,7 +978,6 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
         if (!mbar_wait(smem_u32(&cb.dempty[ts]), tph ^ 1u, deadline) && lane == 0) record_timeout(a);
         const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
         const uint32_t tcol = tmem + lane_addr + ts * acols;
-        const uint32_t ss = smem_u32(&scales[ts]);
         uint32_t qsum[gps];
 #pragma unroll
         for (int g = 0; g < gps; ++g) qsum[g] = 0;
@@ -1019,10 +1010,15 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
 #pragma unroll
           for (int g = 0; g < gps; ++g) qsum[g] += ((c0 * 32) / G == g) ? static_cast<uint32_t>(qs) : 0u;
         }
-        // this K half's share of each group (0 for groups outside the half)
+        // this K half's share of each group (0 for groups outside the half),
+        // one tensor-memory column per group and half: the epilogue reads them
+        // with the accumulators
+        {
+          uint32_t qv[kQCols];
 #pragma unroll
-        for (int g = 0; g < gps; ++g)
-          sts16(ss + offsetof(SlotScales, q) + ((half * kMaxStageGroups + g) * 128 + r) * 2, qsum[g]);
+          for (int g = 0; g < kQCols; ++g) qv[g] = g < gps ? qsum[g] : 0u;
+          tmem_st4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2 + half) * kQCols, qv);
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -1123,7 +1119,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, const OperandMeta* metas,
-                               const SlotScales* scales, const uint8_t* sring, uint64_t deadline) {
+                               const uint8_t* sring, uint64_t deadline) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
@@ -1133,7 +1129,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
   constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   const uint32_t tmem = cb.tmem;
   int ts = 0, xb = 0, sr = 0;
-  uint32_t tph = 0, sph = 0;
+  uint32_t tph = 0;
   int published = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
@@ -1148,14 +1144,15 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 #pragma unroll
       for (int n = 0; n < kFBM; ++n) acc[n] = 0.f;
       for (int s = 0; s < nst; ++s) {
+        // dfull also orders the stage's scales and zero points (they land with
+        // the weight stage, which the dequant warps acquired before the MMA)
+        // and the int4 sums the dequant warps put next to the accumulators
         if (!mbar_wait(smem_u32(&cb.dfull[ts]), tph, deadline) && lane == 0) record_timeout(a);
-        // the slot's int4 sums come from the dequant warps through afull, the
-        // stage's scales and zero points from the producer through sfull
-        if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline) && lane == 0) record_timeout(a);
-        if (!mbar_wait(smem_u32(&cb.sfull[sr]), sph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
         const uint32_t dt = tmem + lane_addr + kTS * acols + ts * dcols;
-        const uint32_t ss = smem_u32(&scales[ts]);
+        uint32_t qh[2][kQCols];
+        tmem_ld4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2) * kQCols, qh[0]);
+        tmem_ld4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2 + 1) * kQCols, qh[1]);
         const uint32_t xs = smem_u32(&meta.xsum[0][0]);
         const uint32_t se = smem_u32(sring + sr * kSRingBytes);
         const bool valid = cb.scale_valid[sr] != 0;
@@ -1169,10 +1166,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         // the scale entry is no longer needed: back to the producer
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&cb.sempty[sr]));
-        if (++sr == kSRing) {
-          sr = 0;
-          sph ^= 1u;
-        }
+        if (++sr == kSRing) sr = 0;
 #pragma unroll
         for (int g = 0; g < gps; ++g) {
           // 256 * D_hi + D_lo' summed over the group's accumulators
@@ -1189,8 +1183,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
           }
           const float sc = scs[g];
           const int z = zs[g];
-          const int q128 = 128 * static_cast<int>(lds16(ss + offsetof(SlotScales, q) + (g * 128 + r) * 2) +
-                                                  lds16(ss + offsetof(SlotScales, q) + ((kMaxStageGroups + g) * 128 + r) * 2));
+          const int q128 = 128 * static_cast<int>(qh[0][g] + qh[1][g]);
           const int gg = s * gps + g;
           const uint4 xa = lds128(xs + gg * kFBM * 4), xb4 = lds128(xs + gg * kFBM * 4 + 16);
           const int xsv[kFBM] = {static_cast<int>(xa.x), static_cast<int>(xa.y), static_cast<int>(xa.z), static_cast<int>(xa.w),
@@ -1253,15 +1246,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
   static_assert(SK / G >= 1 && SK / G <= kAccs && kAccs % (SK / G) == 0, "a stage's groups share the accumulators");
   static_assert(SK / G <= kMaxStageGroups && kTS <= kMaxTSlots, "stage groups and slots fit the control blocks");
-  static_assert(kTS * (SK / 4 + kAccs * 16) <= kTmemCols, "tensor-memory ring fits 512 columns");
+  static_assert(kTS * (SK / 4 + kAccs * 16 + 2 * kQCols) <= kTmemCols, "tensor-memory ring fits 512 columns");
   extern __shared__ __align__(128) uint8_t smem[];
   Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
   int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
   uint8_t* stages = smem + kCtrlBytes + kTableBytes;
   uint8_t* xbufs = stages + static_cast<size_t>(a.stages) * a.stage_bytes;
   OperandMeta* metas = reinterpret_cast<OperandMeta*>(xbufs + 2 * a.xbuf_bytes);
-  SlotScales* scales = reinterpret_cast<SlotScales*>(metas + 2);
-  uint8_t* sring = reinterpret_cast<uint8_t*>(scales + kTS);
+  uint8_t* sring = reinterpret_cast<uint8_t*>(metas + 2);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.stages; ++i) {
@@ -1278,10 +1270,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
       mbar_init(smem_u32(&cb.dfull[i]), 1);
       mbar_init(smem_u32(&cb.dempty[i]), 4);
     }
-    for (int i = 0; i < kSRing; ++i) {
-      mbar_init(smem_u32(&cb.sfull[i]), 1);
-      mbar_init(smem_u32(&cb.sempty[i]), 4);
-    }
+    for (int i = 0; i < kSRing; ++i) mbar_init(smem_u32(&cb.sempty[i]), 4);
     mbar_init(smem_u32(&cb.drain), kMmaIssuers);
     fence_mbar_init();
     cb.gen0 = ld_acquire_gpu(a.bar + 1);
@@ -1303,9 +1292,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   build_table(a, cb, table, reinterpret_cast<int*>(stages));
   // Phase 3: the expert pipeline.
   if (warp < kDQ) {
-    dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, scales, deadline);
+    dequant_warps<SK, G>(a, cb, table, stages, xbufs, metas, deadline);
   } else if (warp < kEpi0 + 4) {
-    epilogue_warps<SK, G>(a, cb, table, metas, scales, sring, deadline);
+    epilogue_warps<SK, G>(a, cb, table, metas, sring, deadline);
   } else if (warp == kMmaWarp || warp == kMmaWarp2) {
     if ((threadIdx.x & 31) == 0) mma_issuer<SK, G>(a, cb, table, xbufs, warp == kMmaWarp2 ? 1 : 0, deadline);
     __syncwarp();
@@ -1389,7 +1378,7 @@ static FusedGeometry geometry_for(int H, int I, int sk) {
   const uint64_t xrow = xq_row_bytes(H) | 16u, hrow = (8ull * I + 16u) | 16u;
   f.xbuf_bytes = round128(static_cast<uint64_t>(kFBM) * (xrow > hrow ? xrow : hrow));
   const size_t fixed = kCtrlBytes + kTableBytes + 2ull * f.xbuf_bytes + 2 * sizeof(OperandMeta) +
-                       tslots_for(sk) * sizeof(SlotScales) + kSRing * kSRingBytes;
+                       kSRing * kSRingBytes;
   const size_t budget = 227 * 1024;
   int s = fixed < budget ? static_cast<int>((budget - fixed) / f.stage_bytes) : 0;
   if (s > kMaxStages) s = kMaxStages;
@@ -1432,7 +1421,7 @@ bool fused_supported(int H, int I, int G) {
   // tensor memory: slots x (A tile + accumulators) <= 512 columns; every
   // group of a stage gets a whole number of the stage's accumulators
   const int ts = tslots_for(f.sk), acc = accs_for(f.sk);
-  if (ts * (f.sk / 4 + acc * 16) > kTmemCols) return false;
+  if (ts * (f.sk / 4 + acc * 16 + 2 * kQCols) > kTmemCols) return false;
   if (f.sk / G > acc || acc % (f.sk / G) || (G / 32) % (acc / (f.sk / G))) return false;
   return f.stages >= kMinStages;
 }
