@@ -334,7 +334,7 @@ def run_prefill_ep(args, rank: int, world: int, dev):
     the gated shared expert at home and an all-to-all combine."""
     import torch
 
-    from mtp_b200 import ExpertParallelMoE
+    from mtp_b200 import ExpertParallelMoE, layer_path
     from mtp_b200.ops import SharedExpert, W4A16Experts
     from mtp_b200.synthetic import CONFIG1, gptq_experts
 
@@ -401,7 +401,12 @@ def run_prefill_ep(args, rank: int, world: int, dev):
         "flops_per_layer": flops,
         "roofline": {"bound": "tensor", "achieved": round(per_gpu_tflops, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(per_gpu_tflops / peak, 4), "peak_source": peak_kind,
-                     "note": "int8 hi/lo MMAs of N=16 (8 pairs) per weight pass: a decode-shaped kernel"},
+                     "note": "useful FLOPs (routed + shared pairs); the kernels also multiply the padding "
+                             "columns of each expert's last 128-pair block"},
+        "kernel_path": {"prefill": "moe_prefill.cu: 128-pair bf16 tcgen05 tiles (router, align, gather, W1, W2, "
+                                   "combine launches)",
+                        "decode": "moe_fused.cu: persistent layer kernel, 8-pair int8 tiles"}[
+                            layer_path(m, epr, cfg.top_k)],
         "dispatch": "NCCL all_to_all_single of bf16 rows (deduplicated per destination) + int32 id/weight lists; "
                     "combine back in bf16, summed in fp32 at home" if world > 1 else "single rank (no exchange)",
         "clocks": clocks.summary(),

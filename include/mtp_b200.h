@@ -205,6 +205,25 @@ MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
 #define MTP_NOALLOC_SCRATCH_BYTES (6u << 20)
 MTP_API int mtp_w4a16_moe_layer_noalloc(const MtpMoeLayerArgs* args, void* stream);
 
+/* ---- the layer forward for prefill-sized calls ------------------------------
+ * Same layer as mtp_w4a16_moe_layer (replaces the same boundary: vLLM
+ * fused_moe W1 -> silu_and_mul -> W2 (MUL_ROUTED_WEIGHT) -> moe_sum as the
+ * reference launches it, tracing/vllm_router_trace.py:19648-19801, plus the
+ * gated shared expert) for calls with many pairs per expert: pairs are blocked
+ * 128 per expert and each block is one bf16 tensor-core tile, the int4 weights
+ * unpacked once per block. Differences from mtp_w4a16_moe_layer: dequantised
+ * weights are rounded to bf16 as the reference's bf16 GEMM does (the
+ * decode kernel keeps them exact), the W2 output per pair is rounded to bf16
+ * before the fp32 top-k sum (vLLM's intermediate_cache3); all experts must be
+ * resident (slot_table == NULL, host_blobs ignored: else MTP_ERR_ARG);
+ * demand_log must be NULL; E + (shared ? 1 : 0) <= 1024. The workspace needs
+ * no zero fill (nothing persists between calls); its size grows with M
+ * (about M * (top_k + 1) * (2 H + I) * 2 bytes plus padding).                */
+MTP_API int mtp_w4a16_moe_prefill_workspace_size(int32_t num_tokens, int32_t num_experts,
+                                         int32_t top_k, int32_t hidden,
+                                         int32_t inter, int64_t* bytes);
+MTP_API int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* args, void* stream);
+
 
 /* ---- MTP expert-demand predictor (prefetch driver) --------------------------
  * logits = W2 . silu(W1 . h + b1) + b2 for each hidden state h [M, hidden]

@@ -14,9 +14,11 @@ from .ops import (  # noqa: F401
     W4A16Experts,
     dequantize_gptq_projection,
     fused_experts,
+    layer_path,
     layer_workspace,
     moe_align_block_size,
     moe_layer_w4a16,
+    prefill_workspace,
     topk_softmax,
 )
 
@@ -30,9 +32,11 @@ __all__ = [
     "W4A16Experts",
     "dequantize_gptq_projection",
     "fused_experts",
+    "layer_path",
     "layer_workspace",
     "moe_align_block_size",
     "moe_layer_w4a16",
     "plan_dispatch",
+    "prefill_workspace",
     "topk_softmax",
 ]

@@ -27,6 +27,8 @@ EXPORTS = (
     "mtp_w4a16_moe_layer_workspace_size",
     "mtp_w4a16_moe_layer",
     "mtp_w4a16_moe_layer_noalloc",
+    "mtp_w4a16_moe_prefill_workspace_size",
+    "mtp_w4a16_moe_prefill",
     "mtp_predictor_pack",
     "mtp_predictor_workspace_size",
     "mtp_predict_topk",
@@ -92,6 +94,8 @@ _SIGS = {
     "mtp_w4a16_moe_layer_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_w4a16_moe_layer": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
     "mtp_w4a16_moe_layer_noalloc": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
+    "mtp_w4a16_moe_prefill_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
+    "mtp_w4a16_moe_prefill": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
     "mtp_predictor_pack": (C.c_int, [vp, i32, i32, vp, vp]),
     "mtp_predictor_workspace_size": (C.c_int, [i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_predict_topk": (C.c_int, [vp, i32, i32, vp, vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, i64, vp]),
@@ -156,6 +160,12 @@ def align_sizes(numel: int, num_experts: int, block_size: int, pad_sorted_ids: b
 def layer_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> int:
     out = i64()
     call("mtp_w4a16_moe_layer_workspace_size", m, e, k, hidden, inter, C.byref(out))
+    return out.value
+
+
+def prefill_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> int:
+    out = i64()
+    call("mtp_w4a16_moe_prefill_workspace_size", m, e, k, hidden, inter, C.byref(out))
     return out.value
 
 

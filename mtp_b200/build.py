@@ -24,7 +24,8 @@ LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libmtp_b200.so"
 STAMP = LIBDIR / "libmtp_b200.stamp"
 
-SOURCES = ["capi.cu", "router_align.cu", "gptq.cu", "moe_fused.cu", "predictor.cu", "prefetch.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "router_align.cu", "gptq.cu", "moe_fused.cu", "moe_prefill.cu", "predictor.cu", "prefetch.cu",
+           "noalloc.cu"]
 HEADERS = ["common.cuh", "internal.cuh", "route.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

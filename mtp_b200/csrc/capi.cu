@@ -247,6 +247,72 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   return launch_moe_fused(f, st);
 }
 
+int mtp_w4a16_moe_prefill_workspace_size(int32_t num_tokens, int32_t num_experts, int32_t top_k,
+                                         int32_t hidden, int32_t inter, int64_t* bytes) {
+  if (!bytes) return MTP_ERR_NULL;
+  if (num_tokens < 1 || num_experts < 1 || top_k < 1 || hidden < 1 || inter < 1) return MTP_ERR_SHAPE;
+  *bytes = prefill_ws(num_tokens, num_experts, top_k, hidden, inter, 1).total;
+  return MTP_OK;
+}
+
+int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* p, void* stream) {
+  if (!p) return MTP_ERR_NULL;
+  const MtpMoeLayerArgs& a = *p;
+  const int M = a.num_tokens, H = a.hidden, I = a.inter, E = a.num_experts, k = a.top_k;
+  const int G = a.group_size;
+  const int has_shared = a.shared_blob ? 1 : 0;
+  if (M < 1 || E < 1 || E + has_shared > 1024 || k < 1 || k > 32 || k > E) return MTP_ERR_SHAPE;
+  if (H < 256 || H > 2048 || H % 256) return MTP_ERR_SHAPE;
+  if (I < 128 || I > 1024 || I % 128) return MTP_ERR_SHAPE;
+  if (G != 64 && G != 128) return MTP_ERR_SHAPE;
+  if (static_cast<int64_t>(M) * (k + 1) > (1LL << 30)) return MTP_ERR_SHAPE;
+  if (a.zero_mode != MTP_ZERO_RAW && a.zero_mode != MTP_ZERO_SYM8) return MTP_ERR_ARG;
+  if (a.slot_table || a.demand_log) return MTP_ERR_ARG;
+  if (!a.hidden_states || !a.out || !a.workspace || !a.expert_blobs) return MTP_ERR_NULL;
+  if (!a.router_logits && (!a.topk_weights || !a.topk_ids)) return MTP_ERR_NULL;
+  if (a.shared_blob && !a.shared_gate_weight) return MTP_ERR_NULL;
+  MtpExpertLayout L;
+  if (expert_layout(H, I, G, &L) != MTP_OK) return MTP_ERR_SHAPE;
+  if (a.expert_bytes < L.bytes) return MTP_ERR_SHAPE;
+  if (!aligned(a.hidden_states, 16) || !aligned(a.out, 16) || !aligned(a.workspace, 256) ||
+      !aligned(a.expert_blobs, 256) || (a.expert_bytes % 256) || (a.shared_blob && !aligned(a.shared_blob, 256)) ||
+      (a.shared_gate_weight && !aligned(a.shared_gate_weight, 16)) || (a.out_f32 && !aligned(a.out_f32, 16)))
+    return MTP_ERR_ALIGN;
+  const PrefillWs w = prefill_ws(M, E, k, H, I, has_shared);
+  if (a.workspace_bytes < w.total) return MTP_ERR_WORKSPACE;
+
+  unsigned char* ws = static_cast<unsigned char*>(a.workspace);
+  PrefillArgs f;
+  f.M = M; f.H = H; f.I = I; f.E = E; f.k = k; f.kx = k + has_shared; f.numel_x = M * f.kx;
+  f.G = G; f.zero_mode = a.zero_mode; f.has_shared = has_shared;
+  f.cap = static_cast<int>(w.cap); f.max_blocks = static_cast<int>(w.max_blocks);
+  f.x = a.hidden_states; f.gate_w = a.shared_gate_weight;
+  if (a.router_logits) {
+    f.topk_w = a.topk_weights_out ? a.topk_weights_out : reinterpret_cast<float*>(ws + w.tw);
+    f.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
+  } else {
+    f.topk_w = a.topk_weights;
+    f.topk_ids = a.topk_ids;
+  }
+  f.ids_x = reinterpret_cast<int32_t*>(ws + w.ids_x);
+  f.w_x = reinterpret_cast<float*>(ws + w.w_x);
+  f.inv = reinterpret_cast<int32_t*>(ws + w.inv);
+  f.sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
+  f.eids = reinterpret_cast<int32_t*>(ws + w.eids);
+  f.ntpp = reinterpret_cast<int32_t*>(ws + w.ntpp);
+  f.pos_tok = reinterpret_cast<int32_t*>(ws + w.pos_tok);
+  f.pos_w = reinterpret_cast<float*>(ws + w.pos_w);
+  f.blk_n = reinterpret_cast<int32_t*>(ws + w.blk_n);
+  f.xg = ws + w.xg;
+  f.hg = ws + w.hg;
+  f.y = reinterpret_cast<uint16_t*>(ws + w.y);
+  f.L = L;
+  f.blobs = a.expert_blobs; f.expert_bytes = a.expert_bytes; f.shared_blob = a.shared_blob;
+  f.out = a.out; f.out_f32 = a.out_f32;
+  f.status = a.status ? a.status : reinterpret_cast<int32_t*>(ws + w.status);
+  return launch_moe_prefill(f, a.renormalize ? 1 : 0, a.router_logits, static_cast<cudaStream_t>(stream));
+}
+
 
 // ---- MTP expert-demand predictor ----------------------------------------------
 int mtp_predictor_pack(const uint16_t* w, int32_t rows, int32_t cols, uint16_t* out, void* stream) {

@@ -75,4 +75,41 @@ bool fused_supported(int H, int I, int G);
 int fused_max_work_segments(int M, int max_seg, int max_blocks);
 int launch_moe_fused(const FusedArgs& a, cudaStream_t st);
 
+// Prefill path (moe_prefill.cu): pairs per expert in blocks of 128.
+struct PrefillArgs {
+  int M, H, I, E, k, kx, numel_x, G, zero_mode, has_shared;
+  int cap, max_blocks;         // sorted capacity and blocks (align sizes for 128-pair blocks)
+  const uint16_t* x;           // [M, H] bf16
+  const uint16_t* gate_w;      // [H] bf16 shared-expert gate or NULL
+  const float* topk_w;         // [M, k]
+  const int32_t* topk_ids;     // [M, k]
+  int32_t* ids_x;              // [M, kx] pairs extended by the shared expert (id E)
+  float* w_x;                  // [M, kx] pair weights (sigmoid gate for the shared expert)
+  int32_t* inv;                // [M, kx] sorted position of each pair, -1 if not routed
+  int32_t* sorted;             // [cap] align output
+  int32_t* eids;               // [max_blocks] expert per block (E = shared)
+  int32_t* ntpp;               // [1] positions used
+  int32_t* pos_tok;            // [cap] token of each position, -1 for padding
+  float* pos_w;                // [cap] weight of each position
+  int32_t* blk_n;              // [max_blocks] valid columns rounded up to 16 (MMA N)
+  uint8_t* xg;                 // [max_blocks] blocks of x rows in the B-operand layout
+  uint8_t* hg;                 // [max_blocks] blocks of h rows in the B-operand layout
+  uint16_t* y;                 // [cap, H] bf16 W2 output times the pair weight
+  MtpExpertLayout L;
+  const uint8_t* blobs;
+  int64_t expert_bytes;
+  const uint8_t* shared_blob;
+  uint16_t* out;
+  float* out_f32;
+  int32_t* status;
+};
+
+struct PrefillWs {
+  int64_t cap, max_blocks;
+  int64_t tw, tid, ids_x, w_x, inv, sorted, eids, ntpp, pos_tok, pos_w, blk_n, status, xg, hg, y, total;
+};
+
+PrefillWs prefill_ws(int M, int E, int k, int H, int I, int has_shared);
+int launch_moe_prefill(PrefillArgs& a, int renorm, const float* logits, cudaStream_t st);
+
 }  // namespace mtp

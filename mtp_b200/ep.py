@@ -124,23 +124,28 @@ class ExpertParallelMoE:
                 group=None, zero_mode: str = "raw") -> "ExpertParallelMoE":
         """``local_experts``: this rank's shard (``W4A16Experts.shard``)."""
         from . import _lib
-        from .ops import layer_workspace, moe_layer_w4a16, topk_softmax
+        from .ops import layer_path, layer_workspace, moe_layer_w4a16, prefill_workspace, topk_softmax
 
         cache = {}
 
-        def workspace(m, dev):
-            # one zero-filled workspace, grown on demand: every call leaves its
-            # counters zero, so calls of any size up to its own can reuse it
-            need = _lib.layer_workspace_bytes(m, local_experts.num_experts, top_k, local_experts.hidden,
-                                              local_experts.inter)
-            ws = cache.get("ws")
+        def workspace(m, dev, path):
+            # one workspace per path, grown on demand: the decode one is
+            # zero-filled once and every call leaves its counters zero, so
+            # calls of any size up to its own can reuse it; the prefill one
+            # keeps nothing between calls
+            size = _lib.prefill_workspace_bytes if path == "prefill" else _lib.layer_workspace_bytes
+            need = size(m, local_experts.num_experts, top_k, local_experts.hidden, local_experts.inter)
+            ws = cache.get(path)
             if ws is None or ws.numel() < need or ws.device != dev:
-                cache["ws"] = ws = layer_workspace(m, local_experts, top_k, dev)
+                make = prefill_workspace if path == "prefill" else layer_workspace
+                cache[path] = ws = make(m, local_experts, top_k, dev)
             return ws
 
         def local_fn(rows, ids, weights):
+            m = rows.shape[0]
+            path = layer_path(m, local_experts.num_experts, top_k)
             return moe_layer_w4a16(rows, None, local_experts, top_k, topk_weights=weights, topk_ids=ids,
-                                   zero_mode=zero_mode, workspace=workspace(rows.shape[0], rows.device))
+                                   zero_mode=zero_mode, workspace=workspace(m, rows.device, path), path=path)
 
         def router_fn(logits, k):
             w, ids, _ = topk_softmax(logits, k, renormalize)
@@ -152,8 +157,11 @@ class ExpertParallelMoE:
                 m = x.shape[0]
                 none_w = torch.zeros((m, top_k), dtype=torch.float32, device=x.device)
                 none_ids = torch.full((m, top_k), -1, dtype=torch.int32, device=x.device)
+                # the shared expert alone: m pairs on one expert
+                path = layer_path(m, 1, 1)
                 return moe_layer_w4a16(x, None, local_experts, top_k, shared=shared, topk_weights=none_w,
-                                       topk_ids=none_ids, zero_mode=zero_mode, workspace=workspace(m, x.device))
+                                       topk_ids=none_ids, zero_mode=zero_mode,
+                                       workspace=workspace(m, x.device, path), path=path)
 
         return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group)
 

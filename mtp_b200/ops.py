@@ -216,6 +216,24 @@ def layer_workspace(m: int, experts: W4A16Experts, top_k: int, device) -> torch.
     return torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
 
+# Average routed pairs per expert from which the automatic path choice runs a
+# call on the prefill kernels (128-pair bf16 tiles) instead of the decode
+# kernel (8-pair int8 tiles, exact dequantisation).
+PREFILL_MIN_PAIRS_PER_EXPERT = 32
+
+
+def layer_path(m: int, num_experts: int, top_k: int) -> str:
+    """"prefill" when the call has enough pairs per expert for 128-pair tiles,
+    else "decode" (the automatic choice of :func:`moe_layer_w4a16`)."""
+    return "prefill" if m * top_k >= PREFILL_MIN_PAIRS_PER_EXPERT * num_experts else "decode"
+
+
+def prefill_workspace(m: int, experts: W4A16Experts, top_k: int, device) -> torch.Tensor:
+    """Workspace of the prefill path (no zero fill needed)."""
+    nbytes = _lib.prefill_workspace_bytes(m, experts.num_experts, top_k, experts.hidden, experts.inter)
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
 def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | None,
                     experts: W4A16Experts, top_k: int, renormalize: bool = True,
                     shared: SharedExpert | None = None, *,
@@ -225,7 +243,7 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
                     out: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,
                     topk_out: tuple[torch.Tensor, torch.Tensor] | None = None,
                     demand_log: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, path: str = "auto") -> torch.Tensor:
     """One W4A16 MoE layer forward: router (when ``router_logits`` is given,
     else the given ``topk_weights``/``topk_ids``), align, gate_up + SiLU*up,
     down + routed weight, top-k sum and the sigmoid-gated shared expert.
@@ -233,7 +251,12 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     Weights: ``experts.blobs`` (slot = expert), or with ``slot_table`` [E]
     int32 the slot cache ``slot_cache`` [S, bytes] (slot -1 = not resident,
     read from the pinned ``host_store`` [E, bytes] through its device
-    mapping). Returns ``out`` [M, H] bf16."""
+    mapping). Returns ``out`` [M, H] bf16.
+
+    ``path``: "decode" (the persistent layer kernel), "prefill" (128-pair
+    bf16 tiles; every expert resident, no ``slot_table`` / ``demand_log``) or
+    "auto": prefill when :func:`layer_path` says so, the call allows it and a
+    given ``workspace`` is large enough for it."""
     _check_cuda("hidden_states", hidden_states, torch.bfloat16, 2)
     m, h = hidden_states.shape
     if h != experts.hidden:
@@ -272,8 +295,18 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
         out = torch.empty((m, h), dtype=torch.bfloat16, device=dev)
     _check_cuda("out", out, torch.bfloat16, 2)
     _check_cuda("out_f32", out_f32, torch.float32, 2)
+    if path not in ("auto", "decode", "prefill"):
+        raise ValueError('path must be "auto", "decode" or "prefill"')
+    if path == "prefill" and (slot_table is not None or demand_log is not None):
+        raise ValueError("the prefill path needs every expert resident and writes no demand_log")
+    if path == "auto":
+        path = "decode"
+        if slot_table is None and demand_log is None and layer_path(m, e, top_k) == "prefill":
+            need = _lib.prefill_workspace_bytes(m, e, top_k, h, experts.inter)
+            if workspace is None or workspace.numel() >= need:
+                path = "prefill"
     if workspace is None:
-        workspace = layer_workspace(m, experts, top_k, dev)
+        workspace = (prefill_workspace if path == "prefill" else layer_workspace)(m, experts, top_k, dev)
     args = _lib.MtpMoeLayerArgs()
     args.num_tokens, args.hidden, args.inter, args.num_experts = m, h, experts.inter, e
     args.top_k, args.group_size, args.renormalize = top_k, experts.group_size, int(bool(renormalize))
@@ -297,7 +330,8 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     args.status = status.data_ptr() if status is not None else None
     args.workspace = workspace.data_ptr()
     args.workspace_bytes = workspace.numel()
-    _lib.call("mtp_w4a16_moe_layer", C.byref(args), _stream(hidden_states))
+    _lib.call("mtp_w4a16_moe_prefill" if path == "prefill" else "mtp_w4a16_moe_layer", C.byref(args),
+              _stream(hidden_states))
     return out
 
 

@@ -76,6 +76,33 @@ def test_argument_errors_need_no_gpu(built_lib):
     assert ws.value > 0
 
 
+def test_prefill_argument_errors_need_no_gpu(built_lib):
+    from mtp_b200 import _lib
+    lib = _lib.load()
+    assert lib.mtp_w4a16_moe_prefill(None, None) == 1
+    args = _lib.MtpMoeLayerArgs()
+    args.num_tokens, args.hidden, args.inter, args.num_experts = 8192, 2048, 512, 256
+    args.top_k, args.group_size = 8, 128
+    assert lib.mtp_w4a16_moe_prefill(C.byref(args), None) == 1                       # NULL buffers
+    table = (C.c_int32 * 256)()
+    args.slot_table = C.cast(table, C.c_void_p)
+    assert lib.mtp_w4a16_moe_prefill(C.byref(args), None) == 9                       # slot table: decode only
+    args.slot_table = None
+    args.inter = 200
+    assert lib.mtp_w4a16_moe_prefill(C.byref(args), None) == 2                       # I not a multiple of 128
+    args.inter, args.num_experts = 512, 1024
+    buf = (C.c_uint8 * 16)()
+    args.shared_blob = C.cast(buf, C.c_void_p)
+    assert lib.mtp_w4a16_moe_prefill(C.byref(args), None) == 2                       # E + shared > 1024
+    # workspace: sorted capacity for 128-pair blocks of E + 1 experts, then the
+    # x / h / y rows of every position
+    ws = C.c_int64()
+    assert lib.mtp_w4a16_moe_prefill_workspace_size(8192, 256, 8, 2048, 512, C.byref(ws)) == 0
+    cap = -(-(8192 * 9 + 257 * 127) // 128) * 128
+    assert ws.value >= cap * (2048 + 512 + 2048) * 2
+    assert ws.value < cap * (2048 + 512 + 2048) * 2 + 64 * cap
+
+
 def test_python_api_rejects_cpu_tensors(built_lib):
     import torch
     import mtp_b200
