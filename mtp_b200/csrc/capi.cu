@@ -303,6 +303,8 @@ int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* p, void* stream) {
   f.pos_tok = reinterpret_cast<int32_t*>(ws + w.pos_tok);
   f.pos_w = reinterpret_cast<float*>(ws + w.pos_w);
   f.blk_n = reinterpret_cast<int32_t*>(ws + w.blk_n);
+  f.hist = reinterpret_cast<int32_t*>(ws + w.hist);
+  f.ebase = reinterpret_cast<int32_t*>(ws + w.ebase);
   f.xg = ws + w.xg;
   f.hg = ws + w.hg;
   f.y = reinterpret_cast<uint16_t*>(ws + w.y);

@@ -92,6 +92,8 @@ struct PrefillArgs {
   int32_t* pos_tok;            // [cap] token of each position, -1 for padding
   float* pos_w;                // [cap] weight of each position
   int32_t* blk_n;              // [max_blocks] valid columns rounded up to 16 (MMA N)
+  int32_t* hist;               // [chunks][E (+1)] align: per-chunk counts, then offsets
+  int32_t* ebase;              // [E (+1)] align: first position of each expert
   uint8_t* xg;                 // [max_blocks] blocks of x rows in the B-operand layout
   uint8_t* hg;                 // [max_blocks] blocks of h rows in the B-operand layout
   uint16_t* y;                 // [cap, H] bf16 W2 output times the pair weight
@@ -105,8 +107,8 @@ struct PrefillArgs {
 };
 
 struct PrefillWs {
-  int64_t cap, max_blocks;
-  int64_t tw, tid, ids_x, w_x, inv, sorted, eids, ntpp, pos_tok, pos_w, blk_n, status, xg, hg, y, total;
+  int64_t cap, max_blocks, nchunks;
+  int64_t tw, tid, ids_x, w_x, inv, sorted, eids, ntpp, pos_tok, pos_w, blk_n, hist, ebase, status, xg, hg, y, total;
 };
 
 PrefillWs prefill_ws(int M, int E, int k, int H, int I, int has_shared);

@@ -12,7 +12,9 @@
 //   prep     one warp per token: the pair lists extended by the shared
 //            expert as expert E (weight sigmoid(x . w_g)), inverse map reset;
 //   align    moe_align_block_size with 128-pair blocks over E (+1) experts
-//            (route.cuh: sorted pair ids, sentinel numel, expert per block);
+//            in three launches (per-chunk expert counts; offsets, padding and
+//            expert per block; a stable scatter per chunk): the canonical
+//            order (pair index ascending inside an expert, sentinel numel);
 //   gather   one CTA per block: the block's x rows into the B-operand layout
 //            (below), each position's token and weight, the valid column
 //            count rounded up to 16 (the MMA's N for that block);
@@ -25,16 +27,16 @@
 //            expert last, of y in fp32).
 //
 // B-operand layout of a block (x for W1, h for W2; K = H or I):
-//   [16 column groups][K/8 chunks][8 columns][8 bf16]: a core matrix (8
-//   columns x 16 bytes) is 128 contiguous bytes, chunks of one group are
-//   128 bytes apart (the descriptor's K-direction offset) and groups K * 16
-//   bytes apart; a stage (128 of K) of one group is one 2 KB range, so a
-//   block with N valid columns needs N / 8 bulk copies per stage.
+//   [K/128 stages][16 column groups][16 chunks][8 columns][8 bf16]: a core
+//   matrix (8 columns x 16 bytes) is 128 contiguous bytes, chunks of one
+//   group are 128 bytes apart (the descriptor's K-direction offset) and
+//   groups 2 KB apart (its N-direction offset); the first N columns of a
+//   stage are one contiguous range of N * 256 bytes, one bulk copy.
 //
 // GEMM kernel (one CTA per SM, 14 warps):
 //   warp 13   producer: per stage, bulk copies of the 128 x 128 int4 weight
 //             tile (8 KB), its scales and zero points, and the block's
-//             N / 8 column groups of the operand into a 4-deep ring;
+//             operand columns into a 4-deep ring;
 //   warps 0-7 dequant: w = bf16((q - z) * bf16(s)) (an exact integer q - z,
 //             one rounding of the product) into tensor memory, lane = weight
 //             row, two k per 32-bit column: the MMA's A operand;
@@ -42,11 +44,13 @@
 //             K = 16; A bf16 from tensor memory, B bf16 from shared memory,
 //             D fp32 in tensor memory) for all stages of a tile into one of
 //             two accumulators, and commits;
-//   warps 8-11 epilogue: tcgen05.ld of the accumulator, then the W1 or W2
-//             output.
+//   warps 8-11 epilogue: tcgen05.ld of the accumulator, then the W1 output
+//             (gate rows handed to the up rows through shared memory) or the
+//             W2 output (staged in shared memory, written 16 bytes a thread).
 // Every wait is bounded by a deadline on the global timer; on expiry the
 // kernel sets bit 0 of status[2] and runs to its end.
 #include "internal.cuh"
+#include "route.cuh"
 
 namespace mtp {
 namespace {
@@ -56,7 +60,8 @@ constexpr int kPSK = 128;            // K per stage
 constexpr int kPStages = 4;          // shared-memory stages = tensor-memory A tiles
 constexpr int kPDq = 8;              // dequant warps 0-7
 constexpr int kPMma = 12;            // MMA issue (and tensor-memory allocation)
-constexpr int kPProd = 13;           // producer; warps 8-11 are the epilogue
+constexpr int kPProd = 13;           // producer
+constexpr int kPEpiWarp0 = 8;        // epilogue warps 8-11
 constexpr int kPThreads = 14 * 32;
 constexpr uint32_t kPWBytes = kPSK / 2 * 128;   // int4 weight tile of a stage
 constexpr uint32_t kPXBytes = kPSK * 2 * kPN;   // operand tile of a stage (bf16)
@@ -64,7 +69,7 @@ constexpr uint32_t kPSBytes = 2 * 256;          // scales of at most two groups
 constexpr uint32_t kPZBytes = 2 * 64;           // zero points of at most two groups
 constexpr uint32_t kPStageBytes = kPWBytes + kPXBytes + kPSBytes + kPZBytes;
 constexpr uint32_t kPCtrl = 1024;
-constexpr uint32_t kPGateBytes = 64 * kPN * 4;  // W1: gate rows handed to the up rows
+constexpr uint32_t kPGateBytes = 64 * kPN * 4;  // W1: gate rows handed to the up rows; W2: y tile
 constexpr uint32_t kPSmem = kPCtrl + kPStages * kPStageBytes + kPGateBytes;
 constexpr int kPACols = kPSK / 2;               // tensor-memory columns of an A tile
 constexpr int kPDCol0 = kPStages * kPACols;     // two accumulators of kPN columns follow
@@ -125,7 +130,8 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillArgs a) 
   if (t >= a.M) return;
   for (int j = lane; j < a.k; j += 32) {
     const int64_t src = static_cast<int64_t>(t) * a.k + j, dst = static_cast<int64_t>(t) * a.kx + j;
-    a.ids_x[dst] = a.topk_ids[src];
+    const int id = a.topk_ids[src];
+    a.ids_x[dst] = id >= 0 && id < a.E ? id : -1;
     a.w_x[dst] = a.topk_w[src];
     a.inv[dst] = -1;
   }
@@ -154,6 +160,95 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillArgs a) 
 }
 
 // ---------------------------------------------------------------------------
+// align over many CTAs: the same output as align_block (route.cuh) for
+// 128-pair blocks, in three launches. Pairs are cut into chunks of kAChunk;
+// `hist` [chunks][ex] holds each chunk's per-expert counts, then (after the
+// offsets launch) each chunk's first position inside its expert's range.
+// ---------------------------------------------------------------------------
+constexpr int kAChunk = 4096;
+
+__device__ __forceinline__ int pair_key(const PrefillArgs& a, int i, int ex) {
+  const int e = a.ids_x[i];
+  return e >= 0 && e < ex ? e : -1;
+}
+
+__global__ void __launch_bounds__(kAlignThreads) prefill_hist_kernel(const PrefillArgs a, int ex) {
+  extern __shared__ int hs[];
+  for (int e = threadIdx.x; e < ex; e += kAlignThreads) hs[e] = 0;
+  __syncthreads();
+  const int i0 = blockIdx.x * kAChunk, i1 = min(i0 + kAChunk, a.numel_x);
+  for (int i = i0 + threadIdx.x; i < i1; i += kAlignThreads) {
+    const int key = pair_key(a, i, ex);
+    if (key >= 0) atomicAdd(&hs[key], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ex; e += kAlignThreads) a.hist[static_cast<int64_t>(blockIdx.x) * ex + e] = hs[e];
+}
+
+// One CTA: expert e's count and its chunks' starting offsets, the padded
+// ranges (exclusive scan over experts), the expert of every block, the
+// sentinel of every padding position and the number of positions used.
+__global__ void __launch_bounds__(kAlignThreads) prefill_offsets_kernel(const PrefillArgs a, int ex, int nchunks) {
+  __shared__ int scan_tmp[32];
+  const int e = threadIdx.x;
+  int cnt = 0;
+  if (e < ex)
+    for (int c = 0; c < nchunks; ++c) {
+      const int64_t at = static_cast<int64_t>(c) * ex + e;
+      const int v = a.hist[at];
+      a.hist[at] = cnt;
+      cnt += v;
+    }
+  const int padded = (cnt + kPN - 1) / kPN * kPN;
+  int total;
+  const int off = block_exclusive_scan(padded, &total, scan_tmp);
+  if (e < ex) {
+    a.ebase[e] = off;
+    for (int b = off / kPN; b < (off + padded) / kPN; ++b) a.eids[b] = e;
+    for (int p = off + cnt; p < off + padded; ++p) a.sorted[p] = a.numel_x;
+  }
+  if (e == 0) *a.ntpp = total;
+}
+
+// Stable scatter of one chunk: pair i goes to its expert's base + the chunk's
+// offset + its rank among the chunk's earlier pairs of that expert.
+__global__ void __launch_bounds__(kAlignThreads) prefill_scatter_kernel(const PrefillArgs a, int ex) {
+  extern __shared__ int sm[];
+  int* run = sm;         // [ex] next position of each expert for this chunk
+  int* wcnt = sm + ex;   // [32][ex] pairs of each expert in each warp of a round
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < ex; e += kAlignThreads)
+    run[e] = a.ebase[e] + a.hist[static_cast<int64_t>(blockIdx.x) * ex + e];
+  for (int x = tid; x < 32 * ex; x += kAlignThreads) wcnt[x] = 0;
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int i0 = blockIdx.x * kAChunk, i1 = min(i0 + kAChunk, a.numel_x);
+  for (int c0 = i0; c0 < i1; c0 += kAlignThreads) {
+    const int i = c0 + tid;
+    const int key = i < i1 ? pair_key(a, i, ex) : -1;
+    const unsigned mask = __match_any_sync(kFullMask, key);
+    const int rank = __popc(mask & lt_mask);
+    const int leader = __ffs(mask) - 1;
+    const int cw = __popc(mask);
+    if (key >= 0 && lane == leader) wcnt[warp * ex + key] = cw;
+    __syncthreads();
+    int base = 0;
+    if (key >= 0 && lane == leader) {
+      base = run[key];
+      for (int w = 0; w < warp; ++w) base += wcnt[w * ex + key];
+    }
+    base = __shfl_sync(kFullMask, base, leader);
+    if (key >= 0) a.sorted[base + rank] = i;
+    __syncthreads();
+    if (key >= 0 && lane == leader) {
+      atomicAdd(&run[key], cw);  // several warps may hold the same expert
+      wcnt[warp * ex + key] = 0;
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // gather: one CTA (256 threads) per block of 128 sorted positions
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) prefill_gather_kernel(const PrefillArgs a) {
@@ -173,9 +268,21 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const PrefillArgs a
   if (threadIdx.x == 0) a.blk_n[blk] = valid <= 16 ? 16 : (valid + 15) / 16 * 16;
   if (tok < 0) return;
   const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tok) * a.H);
-  uint8_t* dst = a.xg + static_cast<int64_t>(blk) * kPN * a.H * 2 + static_cast<int64_t>(n >> 3) * a.H * 16 +
-                 (n & 7) * 16;
-  for (int c = c0; c < a.H / 8; c += 2) *reinterpret_cast<uint4*>(dst + c * 128) = xr[c];
+  uint8_t* dst = a.xg + static_cast<int64_t>(blk) * kPN * a.H * 2 + (n >> 3) * 2048 + (n & 7) * 16;
+  // thread c0 copies the chunks c of its half of the row (chunk c of 8 k:
+  // stage c / 16, offset (c % 16) * 128 inside the column group), eight
+  // consecutive loads (one 128-byte line) in flight
+  const int cb = c0 * (a.H / 16);
+  for (int j0 = 0; j0 < a.H / 16; j0 += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = xr[cb + j0 + j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = cb + j0 + j;
+      *reinterpret_cast<uint4*>(dst + (c >> 4) * 32768 + (c & 15) * 128) = v[j];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -217,8 +324,7 @@ __device__ void prefill_producer(const PrefillArgs& a, PrefillCtrl& cb, uint8_t*
       bulk_g2s(sb, wsrc + static_cast<int64_t>(s) * kPWBytes, kPWBytes, bar);
       bulk_g2s(sb + kPWBytes + kPXBytes, ssrc + static_cast<int64_t>(s) * gps * 256, gps * 256, bar);
       bulk_g2s(sb + kPWBytes + kPXBytes + kPSBytes, zsrc + static_cast<int64_t>(s) * gps * 64, gps * 64, bar);
-      for (int g = 0; g < ngroups; ++g)
-        bulk_g2s(sb + kPWBytes + g * 2048, xsrc + static_cast<int64_t>(g) * K * 16 + s * 2048, 2048, bar);
+      bulk_g2s(sb + kPWBytes, xsrc + static_cast<int64_t>(s) * 32768, ngroups * 2048, bar);
       ++issued;
       if (++st == kPStages) {
         st = 0;
@@ -335,6 +441,13 @@ __device__ void prefill_epilogue(const PrefillArgs& a, PrefillCtrl& cb, float* g
     int blk, rb;
     tile_of<MODE>(a, t, blk, rb);
     const int n = a.blk_n[blk];
+    float wl = 0.f, wnext[kPN / 32];
+    if (MODE == 1) {
+      // the pair weights of the tile's columns, loaded before the wait
+#pragma unroll
+      for (int q = 0; q < kPN / 32; ++q)
+        wnext[q] = 32 * q < n ? a.pos_w[static_cast<int64_t>(blk) * kPN + 32 * q + lane] : 0.f;
+    }
     if (!mbar_wait(smem_u32(&cb.dfull[db]), dph, deadline) && lane == 0) record_ptimeout(a);
     tc_fence_after();
     const uint32_t dt = tmem + (static_cast<uint32_t>(32 * quad) << 16) + kPDCol0 + db * kPN;
@@ -357,7 +470,8 @@ __device__ void prefill_epilogue(const PrefillArgs& a, PrefillCtrl& cb, float* g
         named_bar_sync(kBarPEpi, 128);
         const int i = 32 * (quad - 2) + lane;  // column of h inside the row block
         const int ig = 64 * rb + i;
-        uint8_t* hb = a.hg + static_cast<int64_t>(blk) * kPN * a.I * 2 + (ig >> 3) * 128 + (ig & 7) * 2;
+        uint8_t* hb = a.hg + static_cast<int64_t>(blk) * kPN * a.I * 2 + (ig >> 7) * 32768 + ((ig >> 3) & 15) * 128 +
+                      (ig & 7) * 2;
         for (int c = 0; c < n; c += 16) {
           tmem_ld16(dt + c, v);
           tmem_wait_ld();
@@ -366,7 +480,7 @@ __device__ void prefill_epilogue(const PrefillArgs& a, PrefillCtrl& cb, float* g
             const int col = c + j;
             const float g = gbuf[col * 64 + i];
             const float h = silu_fast(g) * __uint_as_float(v[j]);
-            *reinterpret_cast<__nv_bfloat16*>(hb + static_cast<int64_t>(col >> 3) * a.I * 16 + (col & 7) * 16) =
+            *reinterpret_cast<__nv_bfloat16*>(hb + (col >> 3) * 2048 + (col & 7) * 16) =
                 __float2bfloat16_rn(h);
           }
         }
@@ -376,30 +490,35 @@ __device__ void prefill_epilogue(const PrefillArgs& a, PrefillCtrl& cb, float* g
         named_bar_sync(kBarPEpi, 128);
       }
     } else {
-      const int hrow = 128 * rb + 32 * quad + lane;
-      const int64_t p0 = static_cast<int64_t>(blk) * kPN;
-      uint16_t* yb = a.y + p0 * a.H + hrow;
-      float wl = 0.f;
-      int tl = -1;
-      for (int c = 0; c < n; c += 16) {
-        if ((c & 31) == 0) {
-          wl = a.pos_w[p0 + c + lane];
-          tl = a.pos_tok[p0 + c + lane];
-        }
+      // y rows of the block's positions: the tile (128 rows of H x n columns)
+      // is staged in shared memory as [column][128 rows] bf16, then each
+      // column's 256 contiguous bytes are written with 16-byte stores
+      const int r = 32 * quad + lane;
+      uint16_t* stg = reinterpret_cast<uint16_t*>(gbuf);
+#pragma unroll
+      for (int c = 0; c < kPN; c += 16) {
+        if (c >= n) break;
+        if ((c & 31) == 0) wl = wnext[c >> 5];
         tmem_ld16(dt + c, v);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int src = (c & 16) + j;
-          const float w = __shfl_sync(kFullMask, wl, src);
-          const int tk = __shfl_sync(kFullMask, tl, src);
-          if (tk >= 0)
-            yb[static_cast<int64_t>(c + j) * a.H] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) * w));
+          const float w = __shfl_sync(kFullMask, wl, (c & 16) + j);
+          stg[(c + j) * 128 + r] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j]) * w));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&cb.dempty[db]));
+      named_bar_sync(kBarPEpi, 128);
+      const int et = threadIdx.x - 32 * kPEpiWarp0;
+      uint16_t* yb = a.y + static_cast<int64_t>(blk) * kPN * a.H + 128 * rb;
+      for (int idx = et; idx < n * 16; idx += 128) {
+        const int col = idx >> 4, piece = idx & 15;
+        *reinterpret_cast<uint4*>(yb + static_cast<int64_t>(col) * a.H + piece * 8) =
+            lds128(smem_u32(stg + col * 128 + piece * 8));
+      }
+      named_bar_sync(kBarPEpi, 128);
     }
     if (++db == 2) {
       db = 0;
@@ -516,6 +635,9 @@ PrefillWs prefill_ws(int M, int E, int k, int H, int I, int has_shared) {
   w.pos_tok = take(w.cap * 4);
   w.pos_w = take(w.cap * 4);
   w.blk_n = take(w.max_blocks * 4);
+  w.nchunks = (numel_x + kAChunk - 1) / kAChunk;
+  w.hist = take(w.nchunks * ex * 4);
+  w.ebase = take(ex * 4);
   w.status = take(16);
   w.xg = take(w.cap * H * 2);
   w.hg = take(w.cap * I * 2);
@@ -530,7 +652,9 @@ int launch_moe_prefill(PrefillArgs& a, int renorm, const float* logits, cudaStre
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MTP_ERR_CUDA;
   if (configured_device != dev) {
-    if (cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefill_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(33 * 1024 * sizeof(int))) != cudaSuccess ||
+        cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPSmem)) != cudaSuccess ||
         cudaFuncSetAttribute(prefill_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPSmem)) != cudaSuccess ||
@@ -545,9 +669,11 @@ int launch_moe_prefill(PrefillArgs& a, int renorm, const float* logits, cudaStre
   }
   prefill_prep_kernel<<<(a.M + 7) / 8, 256, 0, st>>>(a);
   if (cudaGetLastError() != cudaSuccess) return MTP_ERR_LAUNCH;
-  const int rc = launch_moe_align(a.ids_x, a.numel_x, a.E + a.has_shared, kPN, nullptr, 0, a.cap, a.max_blocks, 0,
-                                  a.sorted, a.eids, a.ntpp, nullptr, nullptr, st);
-  if (rc != MTP_OK) return rc;
+  const int ex = a.E + a.has_shared;
+  const int nchunks = (a.numel_x + kAChunk - 1) / kAChunk;
+  prefill_hist_kernel<<<nchunks, kAlignThreads, ex * sizeof(int), st>>>(a, ex);
+  prefill_offsets_kernel<<<1, kAlignThreads, 0, st>>>(a, ex, nchunks);
+  prefill_scatter_kernel<<<nchunks, kAlignThreads, 33 * ex * sizeof(int), st>>>(a, ex);
   prefill_gather_kernel<<<a.max_blocks, 256, 0, st>>>(a);
   prefill_gemm_kernel<0><<<num_sms, kPThreads, kPSmem, st>>>(a);
   prefill_gemm_kernel<1><<<num_sms, kPThreads, kPSmem, st>>>(a);
