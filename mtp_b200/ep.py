@@ -105,10 +105,13 @@ class ExpertParallelMoE:
     ``shared_fn(x)`` the gated shared-expert output bf16 [M, H] (or None).
     :meth:`for_gpu` wires them to the CUDA kernels; the tests inject CPU
     versions to check the exchange on gloo ranks. Without an initialised
-    process group the layer runs as a single rank that owns every expert."""
+    process group (or in a group of one) the layer runs as a single rank that
+    owns every expert; ``single_fn(x, logits)``, when given, then computes the
+    whole layer in one call (no dispatch bookkeeping)."""
 
     def __init__(self, num_experts: int, top_k: int, hidden: int, local_fn: Callable,
-                 router_fn: Callable, shared_fn: Callable | None = None, group=None):
+                 router_fn: Callable, shared_fn: Callable | None = None, group=None,
+                 single_fn: Callable | None = None):
         self.world, self.rank = _world(group)
         self.num_experts = num_experts
         self.epr = experts_per_rank(num_experts, self.world)
@@ -118,6 +121,7 @@ class ExpertParallelMoE:
         self.router_fn = router_fn
         self.shared_fn = shared_fn
         self.group = group
+        self.single_fn = single_fn
 
     @classmethod
     def for_gpu(cls, local_experts, num_experts: int, top_k: int, shared=None, renormalize: bool = True,
@@ -163,7 +167,13 @@ class ExpertParallelMoE:
                                        topk_ids=none_ids, zero_mode=zero_mode,
                                        workspace=workspace(m, x.device, path), path=path)
 
-        return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group)
+        def single_fn(x, logits):
+            m = x.shape[0]
+            path = layer_path(m, local_experts.num_experts, top_k)
+            return moe_layer_w4a16(x, logits, local_experts, top_k, renormalize, shared=shared, zero_mode=zero_mode,
+                                   workspace=workspace(m, x.device, path), path=path)
+
+        return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group, single_fn)
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x bf16 [M, H] and router_logits fp32 [M, E] of this rank's tokens -> bf16 [M, H]."""
@@ -173,6 +183,8 @@ class ExpertParallelMoE:
             raise ValueError(f"router_logits must be fp32 [M, {self.num_experts}]")
         m, h, k = x.shape[0], self.hidden, self.top_k
         dev = x.device
+        if self.world == 1 and self.single_fn is not None and m > 0:
+            return self.single_fn(x, router_logits)
         weights, ids = self.router_fn(router_logits, k)
         plan = plan_dispatch(ids, weights, self.num_experts, self.world)
         recv_counts = _exchange_counts(plan.counts, dev, self.group, self.world)

@@ -112,3 +112,18 @@ def test_auto_path_choice(cuda_device):
         mtp_b200.moe_layer_w4a16(x, logits, w, 2, shared=s, path="prefill",
                                  slot_table=torch.arange(8, dtype=torch.int32, device=cuda_device),
                                  slot_cache=w.blobs)
+
+
+def test_expert_parallel_layer_on_one_rank_is_the_layer_call(cuda_device):
+    """Without a process group ExpertParallelMoE runs the whole layer as one
+    call (router, experts, shared expert): the same bits as moe_layer_w4a16."""
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    cfg = LayerConfig(num_experts=8, hidden=512, inter=256, top_k=2, shared=True, tokens=(300,))
+    experts, sh = make_layer(cfg, seed=8)
+    w, s = build(experts, sh, cuda_device)
+    layer = mtp_b200.ExpertParallelMoE.for_gpu(w, 8, 2, shared=s)
+    for m in (5, 300):
+        x, logits = make_inputs(cfg, m, seed=m)
+        x, logits = x.to(cuda_device), logits.to(cuda_device)
+        assert torch.equal(layer(x, logits), mtp_b200.moe_layer_w4a16(x, logits, w, 2, shared=s))
