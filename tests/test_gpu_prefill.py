@@ -127,3 +127,21 @@ def test_expert_parallel_layer_on_one_rank_is_the_layer_call(cuda_device):
         x, logits = make_inputs(cfg, m, seed=m)
         x, logits = x.to(cuda_device), logits.to(cuda_device)
         assert torch.equal(layer(x, logits), mtp_b200.moe_layer_w4a16(x, logits, w, 2, shared=s))
+
+
+def test_prefill_shared_expert_only_call(cuda_device):
+    """The expert-parallel home rank's shared-expert call: every routed id -1,
+    so the only pairs are the shared expert's."""
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    cfg = LayerConfig(num_experts=8, hidden=512, inter=256, top_k=2, shared=True, tokens=(300,))
+    experts, sh = make_layer(cfg, seed=12)
+    w, s = build(experts, sh, cuda_device)
+    x, _ = make_inputs(cfg, 300, seed=13)
+    ids = torch.full((300, 2), -1, dtype=torch.int32, device=cuda_device)
+    wts = torch.zeros((300, 2), dtype=torch.float32, device=cuda_device)
+    out = mtp_b200.moe_layer_w4a16(x.to(cuda_device), None, w, 2, shared=s, topk_weights=wts, topk_ids=ids,
+                                   path="prefill")
+    o = olayer.MoeLayerOracle(experts, sh)
+    ref = o.moe_tokens(x.float(), torch.zeros((300, 2), dtype=torch.long), torch.zeros((300, 2)))
+    check(out, ref)
