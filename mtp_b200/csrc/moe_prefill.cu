@@ -15,9 +15,10 @@
 //            in three launches (per-chunk expert counts; offsets, padding and
 //            expert per block; a stable scatter per chunk): the canonical
 //            order (pair index ascending inside an expert, sentinel numel);
-//   gather   one CTA per block: the block's x rows into the B-operand layout
-//            (below), each position's token and weight, the valid column
-//            count rounded up to 16 (the MMA's N for that block);
+//   gather   one CTA per block: the block's x rows (bulk-copied row by row
+//            into shared memory) into the B-operand layout (below), each
+//            position's token and weight, the valid column count rounded up
+//            to 16 (the MMA's N for that block);
 //   W1       persistent GEMM: tile = (block, row block of 64 gate + 64 up
 //            rows); epilogue writes h = bf16(silu(gate) * up) in the same
 //            B-operand layout for W2;
@@ -249,39 +250,65 @@ __global__ void __launch_bounds__(kAlignThreads) prefill_scatter_kernel(const Pr
 }
 
 // ---------------------------------------------------------------------------
-// gather: one CTA (256 threads) per block of 128 sorted positions
+// gather: one CTA (256 threads) per block of 128 sorted positions. Per stage
+// (128 of K) each valid row's 256 bytes arrive by one 1-D bulk copy (issued by
+// the row's own thread) in a row-major shared tile padded to 272 bytes a row,
+// two stages in flight; the threads then write the stage's first N columns
+// in the B-operand layout with 16-byte loads (conflict-free: 8 rows of a core
+// matrix fall on 8 distinct bank quads) and 16-byte coalesced stores.
 // ---------------------------------------------------------------------------
+constexpr int kGRow = 272;                       // padded bytes per row of the tile
+constexpr uint32_t kGTile = kPN * kGRow;         // one stage
+constexpr uint32_t kGSmem = 2 * kGTile;
+
 __global__ void __launch_bounds__(256) prefill_gather_kernel(const PrefillArgs a) {
+  extern __shared__ __align__(128) uint8_t gsm[];
+  __shared__ uint64_t gbar[2];
   const int blk = blockIdx.x;
   if (blk * kPN >= *a.ntpp) return;
-  const int n = threadIdx.x & (kPN - 1), c0 = threadIdx.x / kPN;
-  const int64_t p = static_cast<int64_t>(blk) * kPN + n;
-  const int pair = a.sorted[p];
+  const int tid = threadIdx.x;
   int tok = -1;
-  if (pair < a.numel_x) tok = pair / a.kx;
-  if (threadIdx.x < kPN) {
+  if (tid < kPN) {
+    const int64_t p = static_cast<int64_t>(blk) * kPN + tid;
+    const int pair = a.sorted[p];
+    if (pair < a.numel_x) tok = pair / a.kx;
     a.pos_tok[p] = tok;
     a.pos_w[p] = tok >= 0 ? a.w_x[pair] : 0.f;
     if (tok >= 0) a.inv[pair] = static_cast<int>(p);
   }
-  const int valid = __syncthreads_count(threadIdx.x < kPN && tok >= 0);
-  if (threadIdx.x == 0) a.blk_n[blk] = valid <= 16 ? 16 : (valid + 15) / 16 * 16;
-  if (tok < 0) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tok) * a.H);
-  uint8_t* dst = a.xg + static_cast<int64_t>(blk) * kPN * a.H * 2 + (n >> 3) * 2048 + (n & 7) * 16;
-  // thread c0 copies the chunks c of its half of the row (chunk c of 8 k:
-  // stage c / 16, offset (c % 16) * 128 inside the column group), eight
-  // consecutive loads (one 128-byte line) in flight
-  const int cb = c0 * (a.H / 16);
-  for (int j0 = 0; j0 < a.H / 16; j0 += 8) {
-    uint4 v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = xr[cb + j0 + j];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = cb + j0 + j;
-      *reinterpret_cast<uint4*>(dst + (c >> 4) * 32768 + (c & 15) * 128) = v[j];
+  if (tid == 0) {
+    mbar_init(smem_u32(&gbar[0]), 1);
+    mbar_init(smem_u32(&gbar[1]), 1);
+    fence_mbar_init();
+  }
+  // valid positions come first in a block (an expert's padding is at its end)
+  const int valid = __syncthreads_count(tid < kPN && tok >= 0);
+  const int n = valid <= 16 ? 16 : (valid + 15) / 16 * 16;
+  if (tid == 0) a.blk_n[blk] = n;
+  const uint64_t deadline = global_timer_ns() + kPTimeoutNs;
+  const int nst = a.H / kPSK;
+  const uint8_t* xrow = tok >= 0 ? reinterpret_cast<const uint8_t*>(a.x) + static_cast<int64_t>(tok) * a.H * 2 : nullptr;
+  uint8_t* dst = a.xg + static_cast<int64_t>(blk) * kPN * a.H * 2;
+  auto issue = [&](int s) {
+    const int b = s & 1;
+    if (tid == 0) mbar_arrive_expect_tx(smem_u32(&gbar[b]), static_cast<uint32_t>(valid) * 256);
+    __syncthreads();
+    if (tok >= 0) bulk_g2s(smem_u32(gsm + b * kGTile + tid * kGRow), xrow + s * 256, 256, smem_u32(&gbar[b]));
+  };
+  issue(0);
+  for (int s = 0; s < nst; ++s) {
+    const int b = s & 1;
+    if (s + 1 < nst) issue(s + 1);
+    if (!mbar_wait(smem_u32(&gbar[b]), static_cast<uint32_t>((s >> 1) & 1), deadline) && tid == 0)
+      atomicOr(a.status + 2, 1);
+    const uint8_t* tile = gsm + b * kGTile;
+    uint8_t* out = dst + static_cast<int64_t>(s) * 32768;
+    for (int idx = tid; idx < n * 16; idx += 256) {
+      // piece idx: column group idx / 128, chunk (idx / 8) % 16, row idx % 8
+      const int row = ((idx >> 7) << 3) | (idx & 7), c = (idx >> 3) & 15;
+      *reinterpret_cast<uint4*>(out + idx * 16) = lds128(smem_u32(tile + row * kGRow + c * 16));
     }
+    __syncthreads();
   }
 }
 
@@ -652,7 +679,9 @@ int launch_moe_prefill(PrefillArgs& a, int renorm, const float* logits, cudaStre
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MTP_ERR_CUDA;
   if (configured_device != dev) {
-    if (cudaFuncSetAttribute(prefill_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefill_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kGSmem)) != cudaSuccess ||
+        cudaFuncSetAttribute(prefill_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(33 * 1024 * sizeof(int))) != cudaSuccess ||
         cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPSmem)) != cudaSuccess ||
@@ -674,7 +703,7 @@ int launch_moe_prefill(PrefillArgs& a, int renorm, const float* logits, cudaStre
   prefill_hist_kernel<<<nchunks, kAlignThreads, ex * sizeof(int), st>>>(a, ex);
   prefill_offsets_kernel<<<1, kAlignThreads, 0, st>>>(a, ex, nchunks);
   prefill_scatter_kernel<<<nchunks, kAlignThreads, 33 * ex * sizeof(int), st>>>(a, ex);
-  prefill_gather_kernel<<<a.max_blocks, 256, 0, st>>>(a);
+  prefill_gather_kernel<<<a.max_blocks, 256, kGSmem, st>>>(a);
   prefill_gemm_kernel<0><<<num_sms, kPThreads, kPSmem, st>>>(a);
   prefill_gemm_kernel<1><<<num_sms, kPThreads, kPSmem, st>>>(a);
   prefill_combine_kernel<<<a.M, a.H / 8, 0, st>>>(a);
