@@ -677,6 +677,10 @@ def main():
 
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        # NVLink SHARP off: the exchange here is all_to_all (no in-switch
+        # reduction to gain), and a rank that dies while bound to an NVLink
+        # multicast object can fault its peers' GPUs.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     res = run_gpu(args, rank, world)
     if rank == 0 and not args.no_cpu:

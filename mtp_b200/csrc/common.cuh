@@ -39,94 +39,6 @@ __device__ __forceinline__ uint4 ldg_stream16(const void* p) {
   return r;
 }
 
-__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
-  uint32_t r;
-  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t ldg_u8(const void* p) {
-  uint16_t r;
-  asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
-}
-
-// ---------------------------------------------------------------------------
-// Tensor-core MMA (m16n8k16, bf16 inputs, fp32 accumulate)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// ---------------------------------------------------------------------------
-// int4 -> bf16 dequantisation by exponent bias
-// ---------------------------------------------------------------------------
-// A bf16 with bit pattern 0x4300 is 128.0 and has 7 mantissa bits, so OR-ing a
-// nibble q (0..15) into its low mantissa bits gives exactly 128 + q. Subtracting
-// the bf16 value 128 + z (same construction) then yields q - z exactly (an
-// integer in [-15, 15] is representable). Two nibbles are handled per 32-bit
-// register: bits [4j, 4j+4) land in the low half, bits [16+4j, 20+4j) in the
-// high half.
-__device__ __forceinline__ uint32_t nib_pair_biased(uint32_t w, int j) {
-  return ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
-}
-
-// Bias constant (128 + z) replicated into both bf16 halves.
-__device__ __forceinline__ uint32_t zero_bias_pair(uint32_t z) {
-  return (0x4300u | (z & 0xFu)) * 0x00010001u;
-}
-
-// One packed weight word -> the four A-fragment registers of an m16n8k16 tile.
-// Word layout (see gptq.cu, kernel layout): nibble j and nibble j+4 are the two
-// elements of A register j; registers 0 and 2 are the thread's row g, 1 and 3
-// its row g+8. One volatile block so the extraction is not hoisted across the
-// whole unrolled K loop (which would hold every dequantised fragment live).
-// lop3 immediate 0xEA = (a & b) | c.
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t zb_lo, uint32_t zb_hi,
-                                             uint32_t (&a)[4]) {
-  asm volatile(
-      "{\n"
-      ".reg .b32 t0, t1, t2, t3;\n"
-      "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n"
-      "shr.u32 t1, %4, 4;\n"
-      "lop3.b32 t1, t1, 0x000F000F, 0x43004300, 0xEA;\n"
-      "shr.u32 t2, %4, 8;\n"
-      "lop3.b32 t2, t2, 0x000F000F, 0x43004300, 0xEA;\n"
-      "shr.u32 t3, %4, 12;\n"
-      "lop3.b32 t3, t3, 0x000F000F, 0x43004300, 0xEA;\n"
-      "sub.rn.bf16x2 %0, t0, %5;\n"
-      "sub.rn.bf16x2 %1, t1, %6;\n"
-      "sub.rn.bf16x2 %2, t2, %5;\n"
-      "sub.rn.bf16x2 %3, t3, %6;\n"
-      "}\n"
-      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-      : "r"(w), "r"(zb_lo), "r"(zb_hi));
-}
-
-// B fragment of an m16n8k16 tile from a k-permuted shared-memory row (see
-// stage_rows_permuted): one 8-byte load gives (b0, b1). Volatile so the load
-// stays next to its MMA rather than being hoisted (register pressure).
-__device__ __forceinline__ void lds_bfrag(const uint16_t* p, uint32_t* b0, uint32_t* b1) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(*b0), "=r"(*b1) : "r"(a));
-}
-
-__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t v) {
-  __half2 h = *reinterpret_cast<__half2*>(&v);
-  return __half22float2(h);
-}
-
-__device__ __forceinline__ float bf16_bits_to_float(uint16_t v) {
-  return __uint_as_float(static_cast<uint32_t>(v) << 16);
-}
-
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
-// x * sigmoid(x) with a fast reciprocal (-> 0 for very negative x)
 // x * sigmoid(x) with the fast exponential and division (a few ulp in fp32;
 // the result is rounded to bf16 by its callers). For x < -87, exp(-x) is inf
 // and the quotient is -0.
@@ -262,85 +174,11 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// ldmatrix x4: B fragments of two consecutive k16 steps from 8 bf16 rows.
-// Lanes 8i..8i+7 give the row addresses of matrix i (row n = lane & 7 at
-// k offset 8i). Volatile so it stays next to its MMAs.
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-// int8 MMA m16n8k32, exact int32 accumulation: A = unsigned 4-bit weights held
-// as u8, B = the high (signed) or low (unsigned) byte of 16-bit activations.
-__device__ __forceinline__ void imma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void imma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void imma_u8s8_zc(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
-}
-__device__ __forceinline__ void imma_u8u8_zc(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
-}
-
-// Two packed weight words (row g and row g+8 of one k32 step, kernel layout in
-// gptq.cu) -> the four u8 A registers of an m16n8k32 tile: the low nibbles of
-// each byte are k = 4t..4t+3, the high nibbles k = 16+4t..16+4t+3. One
-// volatile block so it is not hoisted across the unrolled loop.
-__device__ __forceinline__ void unpack_u8(uint32_t wg, uint32_t wg8, uint32_t (&a)[4]) {
-  asm volatile(
-      "{\n"
-      ".reg .b32 t0, t1;\n"
-      "and.b32 %0, %4, 0x0F0F0F0F;\n"
-      "and.b32 %1, %5, 0x0F0F0F0F;\n"
-      "shr.u32 t0, %4, 4;\n"
-      "shr.u32 t1, %5, 4;\n"
-      "and.b32 %2, t0, 0x0F0F0F0F;\n"
-      "and.b32 %3, t1, 0x0F0F0F0F;\n"
-      "}\n"
-      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-      : "r"(wg), "r"(wg8));
-}
-
-// MMA with a zero C operand (starts a fresh per-chunk partial).
-__device__ __forceinline__ void mma_bf16_16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                                  uint32_t b1) {
-  const float z = 0.f;
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
-}
-
 
 // ---------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores): tensor memory, MMA, commit

@@ -299,8 +299,18 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const PrefillArgs a
   for (int s = 0; s < nst; ++s) {
     const int b = s & 1;
     if (s + 1 < nst) issue(s + 1);
-    if (!mbar_wait(smem_u32(&gbar[b]), static_cast<uint32_t>((s >> 1) & 1), deadline) && tid == 0)
-      atomicOr(a.status + 2, 1);
+    const bool landed = mbar_wait(smem_u32(&gbar[b]), static_cast<uint32_t>((s >> 1) & 1), deadline);
+    if (__syncthreads_or(!landed)) {
+      // Timed out: issue nothing more, and before the CTA (and its shared
+      // memory) goes away give the copies still in flight into both buffers,
+      // stage s and stage s + 1, one more bounded wait.
+      if (tid == 0) atomicOr(a.status + 2, 1);
+      const uint64_t drain = global_timer_ns() + kPTimeoutNs;
+      mbar_wait(smem_u32(&gbar[b]), static_cast<uint32_t>((s >> 1) & 1), drain);
+      if (s + 1 < nst) mbar_wait(smem_u32(&gbar[b ^ 1]), static_cast<uint32_t>(((s + 1) >> 1) & 1), drain);
+      __syncthreads();
+      return;
+    }
     const uint8_t* tile = gsm + b * kGTile;
     uint8_t* out = dst + static_cast<int64_t>(s) * 32768;
     for (int idx = tid; idx < n * 16; idx += 256) {

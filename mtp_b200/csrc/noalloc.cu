@@ -17,7 +17,11 @@
 // The array's name is only a host-side stand-in in host code, so its device
 // address is looked up with cudaGetSymbolAddress, once per device, with that
 // device current, on the first call made on that device; that first call
-// should therefore come before any stream capture. All calls share the one
+// should therefore come before any stream capture. The address is kept for
+// the life of the process, keyed by device index: after cudaDeviceReset (or
+// any teardown of the device's primary context) it is stale, so a process
+// that resets a device must not call this entry point on it again. All calls
+// share the one
 // array and it keeps the last call's contents: the counters that must start
 // at zero are zero when the library loads (a __device__ array starts zeroed)
 // and every completed call leaves them zero again; everything else is written

@@ -19,7 +19,13 @@ KEYS = ("w13_qweight", "w13_qzeros", "w13_scales", "w2_qweight", "w2_qzeros", "w
 
 
 def _init(backend: str, rank: int, world: int, port: int):
+    import os
+
     import torch.distributed as dist
+    # NVLink SHARP off: a rank that dies while its memory is bound to an NVLink
+    # multicast object can fault the other ranks' GPUs, and the test harness
+    # ends ranks that do not exit in time.
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
 

@@ -18,8 +18,6 @@ from oracle import layer as olayer
 pytestmark = pytest.mark.gpu
 
 KEYS = ("w13_qweight", "w13_qzeros", "w13_scales", "w2_qweight", "w2_qzeros", "w2_scales")
-REL_L2 = 1e-2          # the layer tolerance the other GPU tests use
-NORM_MAX_ABS = 2e-2
 
 
 def _args(x, logits, experts, shared, out, k=8):
@@ -67,8 +65,11 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda_device, layer, m):
         assert status == 0, lib.mtp_status_string(status)
         torch.cuda.synchronize()
         assert torch.isfinite(out.float()).all()
-        assert olayer.relative_l2(out.float().cpu(), ref.float().cpu()) <= REL_L2
-        assert olayer.normalized_max_abs(out.float().cpu(), ref.float().cpu()) <= NORM_MAX_ABS
+        # the layer is deterministic: the same call on other scratch memory
+        # gives the same bits
+        assert torch.equal(out, ref), (
+            f"rel-L2 {olayer.relative_l2(out.float().cpu(), ref.float().cpu()):.3e}, "
+            f"normalised max-abs {olayer.normalized_max_abs(out.float().cpu(), ref.float().cpu()):.3e}")
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device, layer):
