@@ -179,8 +179,8 @@ typedef struct MtpMoeLayerArgs {
                                       bytes, ZERO-FILLED before its first use:
                                       the layer keeps its per-call counters
                                       there and every call leaves them zero
-                                      again (re-zero it after a call that
-                                      reported a timeout in status[2])       */
+                                      again, a call whose waits timed out
+                                      included (see _timeouts below)         */
   int64_t workspace_bytes;
 } MtpMoeLayerArgs;
 
@@ -188,6 +188,14 @@ MTP_API int mtp_w4a16_moe_layer_workspace_size(int32_t num_tokens, int32_t num_e
                                        int32_t top_k, int32_t hidden,
                                        int32_t inter, int64_t* bytes);
 MTP_API int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* args, void* stream);
+
+/* Number of calls on this layer workspace whose bounded waits ran out (each
+ * such call also sets bit 0 of status[2] when `status` is given, and leaves
+ * a wrong output). The workspace repairs itself: the last CTA of such a call
+ * clears every counter, so the next call is correct. Copies the count to the
+ * host and synchronises `stream`. No counterpart in the reference (its
+ * kernels have no bounded waits).                                           */
+MTP_API int mtp_w4a16_moe_layer_timeouts(const void* workspace, int32_t* count, void* stream);
 
 /* ---- the layer forward without a caller-provided workspace ------------------
  * No counterpart in the reference: an addition for callers that cannot
@@ -223,6 +231,24 @@ MTP_API int mtp_w4a16_moe_prefill_workspace_size(int32_t num_tokens, int32_t num
                                          int32_t top_k, int32_t hidden,
                                          int32_t inter, int64_t* bytes);
 MTP_API int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* args, void* stream);
+
+/* Where a prefill call leaves its align tables in its workspace (byte offsets),
+ * for inspection: the pairs extended by the shared expert (pair_expert_ids
+ * [M, pairs_per_token] int32, the shared expert as id E, -1 for ids outside
+ * [0, E)), and the moe_align_block_size result over them with block_size 128
+ * and E (+1) experts: sorted_token_ids [capacity] (pair indices, sentinel
+ * M * pairs_per_token, valid up to num_tokens_post_padded), expert_ids
+ * [max_blocks] (valid for the first num_tokens_post_padded / 128 blocks),
+ * num_tokens_post_padded [1]. Same contract as mtp_moe_align (vLLM
+ * fused_moe/moe_align_block_size.py, called at
+ * tracing/vllm_router_trace.py:19648-19659) with pad_sorted_ids.           */
+typedef struct MtpPrefillTables {
+  int64_t pair_expert_ids, sorted_token_ids, expert_ids, num_tokens_post_padded;
+  int32_t capacity, max_blocks, pairs_per_token, block_size;
+} MtpPrefillTables;
+MTP_API int mtp_w4a16_moe_prefill_tables(int32_t num_tokens, int32_t num_experts, int32_t top_k,
+                                         int32_t hidden, int32_t inter, int32_t has_shared,
+                                         MtpPrefillTables* out);
 
 
 /* ---- MTP expert-demand predictor (prefetch driver) --------------------------

@@ -26,9 +26,11 @@ EXPORTS = (
     "mtp_w4a16_repack_gptq",
     "mtp_w4a16_moe_layer_workspace_size",
     "mtp_w4a16_moe_layer",
+    "mtp_w4a16_moe_layer_timeouts",
     "mtp_w4a16_moe_layer_noalloc",
     "mtp_w4a16_moe_prefill_workspace_size",
     "mtp_w4a16_moe_prefill",
+    "mtp_w4a16_moe_prefill_tables",
     "mtp_predictor_pack",
     "mtp_predictor_workspace_size",
     "mtp_predict_topk",
@@ -66,6 +68,12 @@ class MtpMoeLayerArgs(C.Structure):
     ]
 
 
+class MtpPrefillTables(C.Structure):
+    _fields_ = [("pair_expert_ids", i64), ("sorted_token_ids", i64), ("expert_ids", i64),
+                ("num_tokens_post_padded", i64), ("capacity", i32), ("max_blocks", i32),
+                ("pairs_per_token", i32), ("block_size", i32)]
+
+
 class MtpPrefetchConfig(C.Structure):
     _fields_ = [("device", i32), ("num_layers", i32), ("num_experts", i32), ("slots_per_layer", i32),
                 ("expert_bytes", i64), ("host_store", vp), ("cache_base", vp), ("slot_tables", vp),
@@ -94,6 +102,8 @@ _SIGS = {
     "mtp_w4a16_moe_layer_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_w4a16_moe_layer": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
     "mtp_w4a16_moe_layer_noalloc": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
+    "mtp_w4a16_moe_layer_timeouts": (C.c_int, [vp, C.POINTER(i32), vp]),
+    "mtp_w4a16_moe_prefill_tables": (C.c_int, [i32, i32, i32, i32, i32, i32, C.POINTER(MtpPrefillTables)]),
     "mtp_w4a16_moe_prefill_workspace_size": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_w4a16_moe_prefill": (C.c_int, [C.POINTER(MtpMoeLayerArgs), vp]),
     "mtp_predictor_pack": (C.c_int, [vp, i32, i32, vp, vp]),
@@ -161,6 +171,12 @@ def layer_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> in
     out = i64()
     call("mtp_w4a16_moe_layer_workspace_size", m, e, k, hidden, inter, C.byref(out))
     return out.value
+
+
+def prefill_tables(m: int, e: int, k: int, hidden: int, inter: int, has_shared: bool) -> MtpPrefillTables:
+    out = MtpPrefillTables()
+    call("mtp_w4a16_moe_prefill_tables", m, e, k, hidden, inter, int(has_shared), C.byref(out))
+    return out
 
 
 def prefill_workspace_bytes(m: int, e: int, k: int, hidden: int, inter: int) -> int:

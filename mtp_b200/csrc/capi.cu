@@ -27,9 +27,8 @@ static AlignSizes align_sizes(int numel, int E, int BM, int pad) {
 // regions (grid barrier, per-expert counts, per-segment counters) have fixed
 // offsets and sizes, the same for every call shape, so one workspace can serve
 // calls of any size: they must be zero before the first call, and every call
-// that completes leaves them zero again.
-constexpr int kMaxExpertsWs = 1024;
-constexpr int kMaxWorkSegments = 32768;
+// leaves them zero again (after a call whose waits timed out, its last CTA
+// clears them in full).
 struct LayerWs {
   int64_t bar, cnt, seg_done, tw, tid, lists, gate, xq, wseg, status, gu, ybuf, total;
   int max_ws;
@@ -46,7 +45,7 @@ static LayerWs layer_ws(int M, int E, int k, int H, int I) {
     o = round_up(o + bytes, 256);
     return at;
   };
-  w.bar = take(8);
+  w.bar = take(32);
   w.cnt = take(4LL * kMaxExpertsWs);
   w.seg_done = take(4LL * kMaxWorkSegments);
   w.tw = take(4LL * numel);
@@ -245,6 +244,38 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
   f.demand_log = a.demand_log;
   f.stages = 0; f.sk = 0; f.stage_bytes = 0; f.xbuf_bytes = 0;
   return launch_moe_fused(f, st);
+}
+
+int mtp_w4a16_moe_layer_timeouts(const void* workspace, int32_t* count, void* stream) {
+  if (!workspace || !count) return MTP_ERR_NULL;
+  if (!aligned(workspace, 256)) return MTP_ERR_ALIGN;
+  // bar[4] of the fixed counter region (see finish_call in moe_fused.cu)
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, static_cast<const int32_t*>(workspace) + 4, sizeof(v), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return MTP_ERR_CUDA;
+  }
+  *count = v;
+  return MTP_OK;
+}
+
+int mtp_w4a16_moe_prefill_tables(int32_t num_tokens, int32_t num_experts, int32_t top_k, int32_t hidden,
+                                 int32_t inter, int32_t has_shared, MtpPrefillTables* out) {
+  if (!out) return MTP_ERR_NULL;
+  if (num_tokens < 1 || num_experts < 1 || top_k < 1 || hidden < 1 || inter < 1) return MTP_ERR_SHAPE;
+  const PrefillWs w = prefill_ws(num_tokens, num_experts, top_k, hidden, inter, has_shared ? 1 : 0);
+  out->pair_expert_ids = w.ids_x;
+  out->sorted_token_ids = w.sorted;
+  out->expert_ids = w.eids;
+  out->num_tokens_post_padded = w.ntpp;
+  out->capacity = static_cast<int32_t>(w.cap);
+  out->max_blocks = static_cast<int32_t>(w.max_blocks);
+  out->pairs_per_token = top_k + (has_shared ? 1 : 0);
+  out->block_size = static_cast<int32_t>(w.cap / w.max_blocks);
+  return MTP_OK;
 }
 
 int mtp_w4a16_moe_prefill_workspace_size(int32_t num_tokens, int32_t num_experts, int32_t top_k,

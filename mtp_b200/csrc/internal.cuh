@@ -39,7 +39,8 @@ struct FusedArgs {
   const uint8_t* shared_blob;
   float* gate;               // [M] sigmoid(x . w_g)
   uint8_t* xq;               // [M][xq_row_bytes(H)] quantised x rows, see xq_row_bytes
-  int32_t* bar;              // [2] grid barrier (count, generation)    \ zero before the first
+  int32_t* bar;              // [8] grid barrier (count, generation),   \ zero before the first
+                             //     CTAs done, dirty flag, timeouts seen |
   int32_t* cnt;              // [E] pairs per expert                    |  call; every call
   int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero
   int32_t* lists;            // [E][M] pair ids per expert
@@ -53,6 +54,10 @@ struct FusedArgs {
   uint32_t stage_bytes;
   uint32_t xbuf_bytes;
 };
+
+// Fixed counter regions of the layer workspace (see capi.cu layer_ws).
+constexpr int kMaxExpertsWs = 1024;
+constexpr int kMaxWorkSegments = 32768;
 
 int launch_router_topk(const float* logits, int M, int E, int k, int renorm, float* w,
                        int32_t* ids, int32_t* tei, cudaStream_t st);

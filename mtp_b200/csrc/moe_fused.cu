@@ -81,19 +81,28 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
 constexpr int kMaxStages = 8;
-constexpr int kMaxTSlots = 4;       // tensor-memory ring slots (at most)
-// Per K-per-stage choices: tensor-memory ring slots (A tile of SK / 4 columns
-// plus the accumulators) and independent accumulators per stage (16 columns
-// each, at least one per quantisation group of the stage).
+constexpr int kMaxASlots = 4;
+constexpr int kMaxDSlots = 8;
+constexpr int kQCols = 4;
+constexpr int kTmemCols = 512;
+__host__ __device__ constexpr int accs_for(int sk) { return sk >= 512 ? 4 : 2; }
+__host__ __device__ constexpr int aslots_for(int sk) { return sk >= 512 ? 2 : 4; }
+__host__ __device__ constexpr int dslot_cols(int sk) { return accs_for(sk) * 16 + 2 * kQCols; }
+__host__ __device__ constexpr int dslots_for(int sk) {
+  return (kTmemCols - aslots_for(sk) * (sk / 4)) / dslot_cols(sk) < kMaxDSlots
+             ? (kTmemCols - aslots_for(sk) * (sk / 4)) / dslot_cols(sk)
+             : kMaxDSlots;
+}
 template <int SK>
 struct StageCfg {
-  static constexpr int tslots = SK >= 512 ? 2 : 4;
-  static constexpr int accs = SK >= 512 ? 4 : 2;
+  static constexpr int accs = accs_for(SK);
+  static constexpr int aslots = aslots_for(SK);
+  static constexpr int dslots = dslots_for(SK);
+  static constexpr uint32_t acols = SK / 4;
+  static constexpr uint32_t dcols = accs * 16;
+  static constexpr uint32_t dbase = aslots * acols;
+  static constexpr uint32_t dstride = dslot_cols(SK);
 };
-__host__ __device__ constexpr int tslots_for(int sk) { return sk >= 512 ? 2 : 4; }
-constexpr int kQCols = 4;  // tensor-memory columns per slot for the rows' int4 sums per group
-__host__ __device__ constexpr int accs_for(int sk) { return sk >= 512 ? 4 : 2; }
-constexpr int kTmemCols = 512;
 constexpr int kCtrlBytes = 1024;
 constexpr int kWsCache = 64;        // work segments cached in shared memory per pass
 constexpr int kTableBytes = 2 * kWsCache * kWsInts * 4;
@@ -117,9 +126,10 @@ struct Ctrl {
   uint64_t xfull[2];            // operand rows landed
   uint64_t xempty[2];           // operand buffer free (one commit per MMA issuer + 4 epilogue warps)
   uint64_t qfull[2];            // operand quantised (B operand ready)
-  uint64_t afull[kMaxTSlots];   // A tile of a tensor-memory slot written
-  uint64_t dfull[kMaxTSlots];   // accumulators of a slot complete (MMA commit)
-  uint64_t dempty[kMaxTSlots];  // accumulators of a slot read by the epilogue
+  uint64_t afull[kMaxASlots];
+  uint64_t aempty[kMaxASlots];
+  uint64_t dfull[kMaxDSlots];
+  uint64_t dempty[kMaxDSlots];
   uint64_t drain;               // final MMA commit
   uint64_t sempty[kSRing];      // scale entry read by the 4 epilogue warps
   int scale_valid[kSRing];      // 0: the stage's expert has no weights (its terms are zero)
@@ -127,6 +137,7 @@ struct Ctrl {
   int cached[2];      // 1 if the pass range's segments are in the table
   int S;              // work segments of this call
   int gen0;           // grid-barrier generation when the kernel started
+  int last;           // 1 in the CTA that finished last
   uint32_t tmem;      // tensor-memory base address
   int scan[32];       // block-scan scratch
 };
@@ -193,7 +204,41 @@ __device__ __forceinline__ bool reuses_operand(const Pass& P, int u) {
   return s == (u - 1) / P.per && ws_entry(P, s)[2] == 1;
 }
 
-__device__ __forceinline__ void record_timeout(const FusedArgs& a) { atomicOr(a.status + 2, 1); }
+// A wait ran out: report it (status bit 0) and mark the workspace so that the
+// CTA finishing last clears every counter region for the next call.
+__device__ __forceinline__ void record_timeout(const FusedArgs& a) {
+  atomicOr(a.status + 2, 1);
+  atomicExch(a.bar + 3, 1);
+}
+
+// The CTA that finishes last (arrival counter bar[2]) checks the dirty flag
+// bar[3]: after a call in which any wait ran out, counters may be left
+// anywhere (a barrier that gave up, late arrivals), so it clears every
+// counter region in full, counts the event in bar[4] and rearms the flag.
+// One timed-out call therefore does not disturb the next.
+__device__ void finish_call(const FusedArgs& a, int* last_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    *last_flag = atom_acq_rel_gpu_add(a.bar + 2, 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!*last_flag) return;
+  if (ld_acquire_gpu(a.bar + 3) != 0) {
+    for (int i = threadIdx.x; i < kMaxExpertsWs; i += blockDim.x) a.cnt[i] = 0;
+    for (int i = threadIdx.x; i < kMaxWorkSegments; i += blockDim.x) a.seg_done[i] = 0;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      a.bar[0] = 0;
+      a.bar[4] += 1;
+      a.bar[3] = 0;
+    }
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    a.bar[2] = 0;
+  }
+}
 
 // Grid-wide barrier over the kernel's CTAs (all resident: one per SM). One
 // thread per CTA calls it; the generation word a.bar[1] counts completed
@@ -952,12 +997,11 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
   const int r = 32 * quad + lane;  // weight row = tensor-memory lane
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
   constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
-  constexpr uint32_t acols = SK / 4, dcols = StageCfg<SK>::accs * 16;
-  constexpr int kTS = StageCfg<SK>::tslots;
+  using C = StageCfg<SK>;
   static_assert(gps <= kQCols, "a stage's groups fit the sum columns");
   const uint32_t tmem = cb.tmem;
-  int st = 0, ts = 0, xb = 0;
-  uint32_t ph = 0, tph = 0, xph = 0;
+  int st = 0, ta = 0, td = 0, xb = 0;
+  uint32_t ph = 0, aph = 0, dph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int K = pass == 0 ? a.H : a.I;
@@ -975,9 +1019,10 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
       }
       for (int s = 0; s < nst; ++s) {
         if (!mbar_wait(smem_u32(&cb.full[st]), ph, deadline) && lane == 0) record_timeout(a);
-        if (!mbar_wait(smem_u32(&cb.dempty[ts]), tph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        if (!mbar_wait(smem_u32(&cb.aempty[ta]), aph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        tc_fence_after();
         const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
-        const uint32_t tcol = tmem + lane_addr + ts * acols;
+        const uint32_t tcol = tmem + lane_addr + ta * C::acols;
         uint32_t qsum[gps];
 #pragma unroll
         for (int g = 0; g < gps; ++g) qsum[g] = 0;
@@ -1013,23 +1058,29 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
         // this K half's share of each group (0 for groups outside the half),
         // one tensor-memory column per group and half: the epilogue reads them
         // with the accumulators
+        if (!mbar_wait(smem_u32(&cb.dempty[td]), dph ^ 1u, deadline) && lane == 0) record_timeout(a);
+        tc_fence_after();
         {
           uint32_t qv[kQCols];
 #pragma unroll
           for (int g = 0; g < kQCols; ++g) qv[g] = g < gps ? qsum[g] : 0u;
-          tmem_st4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2 + half) * kQCols, qv);
+          tmem_st4(tmem + lane_addr + C::dbase + td * C::dstride + C::dcols + half * kQCols, qv);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&cb.afull[ts]));
+        if (lane == 0) mbar_arrive(smem_u32(&cb.afull[ta]));
         if (++st == a.stages) {
           st = 0;
           ph ^= 1u;
         }
-        if (++ts == kTS) {
-          ts = 0;
-          tph ^= 1u;
+        if (++ta == C::aslots) {
+          ta = 0;
+          aph ^= 1u;
+        }
+        if (++td == C::dslots) {
+          td = 0;
+          dph ^= 1u;
         }
       }
       if (!keep) {
@@ -1054,12 +1105,12 @@ template <int SK, int G>
 __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8_t* xbufs, int which,
                            uint64_t deadline) {
   constexpr int chunks = SK / 32;
-  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
-  constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
+  using C = StageCfg<SK>;
+  constexpr int kAccs = C::accs;
   constexpr int cpg = G / 32, subs = kAccs / (SK / G);
   const uint32_t tmem = cb.tmem;
-  int ts = 0, xb = 0, g = 0;
-  uint32_t tph = 0, xph = 0;
+  int ta = 0, td = 0, xb = 0, g = 0;
+  uint32_t aph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int K = pass == 0 ? a.H : a.I;
@@ -1070,17 +1121,18 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
       if (!reuse && !mbar_wait(smem_u32(&cb.qfull[xb]), xph, deadline)) record_timeout(a);
       const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
       for (int s = 0; s < nst; ++s, ++g) {
-        if ((g & 1) != which) {  // the other issuer's stage
-          if (++ts == kTS) {
-            ts = 0;
-            tph ^= 1u;
-          }
-          continue;
+        const int ta_s = ta, td_s = td;
+        const uint32_t aph_s = aph;
+        if (++ta == C::aslots) {
+          ta = 0;
+          aph ^= 1u;
         }
-        if (!mbar_wait(smem_u32(&cb.afull[ts]), tph, deadline)) record_timeout(a);
+        if (++td == C::dslots) td = 0;
+        if ((g & 1) != which) continue;
+        if (!mbar_wait(smem_u32(&cb.afull[ta_s]), aph_s, deadline)) record_timeout(a);
         tc_fence_after();
-        const uint32_t a_t = tmem + ts * acols;
-        const uint32_t d_t = tmem + kTS * acols + ts * dcols;
+        const uint32_t a_t = tmem + ta_s * C::acols;
+        const uint32_t d_t = tmem + C::dbase + td_s * C::dstride;
         // B: 16 rows = the high plane's 8 rows, then (SBO = 8K bytes on) the low
         // plane's; chunk c of 32 k starts 256 bytes further (start field +16).
         // kAccs independent accumulators per stage, issued round robin, so an
@@ -1095,11 +1147,8 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
             umma_i8_ts(d_t + d * 16, a_t + c * 8, desc0 + 16 * c, kIdesc, t != 0);
           }
         }
-        umma_commit(smem_u32(&cb.dfull[ts]));
-        if (++ts == kTS) {
-          ts = 0;
-          tph ^= 1u;
-        }
+        umma_commit(smem_u32(&cb.aempty[ta_s]));
+        umma_commit(smem_u32(&cb.dfull[td_s]));
       }
       if (!keep) {
         umma_commit(smem_u32(&cb.xempty[xb]));
@@ -1124,12 +1173,12 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
   const int quad = warp & 3;
   const int r = 32 * quad + lane;  // accumulator row = tensor-memory lane
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
-  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
+  using C = StageCfg<SK>;
+  constexpr int kAccs = C::accs;
   constexpr int gps = SK / G, subs = kAccs / gps;
-  constexpr uint32_t acols = SK / 4, dcols = kAccs * 16;
   const uint32_t tmem = cb.tmem;
-  int ts = 0, xb = 0, sr = 0;
-  uint32_t tph = 0;
+  int td = 0, xb = 0, sr = 0;
+  uint32_t dph = 0;
   int published = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
@@ -1147,12 +1196,12 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         // dfull also orders the stage's scales and zero points (they land with
         // the weight stage, which the dequant warps acquired before the MMA)
         // and the int4 sums the dequant warps put next to the accumulators
-        if (!mbar_wait(smem_u32(&cb.dfull[ts]), tph, deadline) && lane == 0) record_timeout(a);
+        if (!mbar_wait(smem_u32(&cb.dfull[td]), dph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
-        const uint32_t dt = tmem + lane_addr + kTS * acols + ts * dcols;
+        const uint32_t dt = tmem + lane_addr + C::dbase + td * C::dstride;
         uint32_t qh[2][kQCols];
-        tmem_ld4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2) * kQCols, qh[0]);
-        tmem_ld4(tmem + lane_addr + kTS * (acols + dcols) + (ts * 2 + 1) * kQCols, qh[1]);
+        tmem_ld4(dt + C::dcols, qh[0]);
+        tmem_ld4(dt + C::dcols + kQCols, qh[1]);
         const uint32_t xs = smem_u32(&meta.xsum[0][0]);
         const uint32_t se = smem_u32(sring + sr * kSRingBytes);
         const bool valid = cb.scale_valid[sr] != 0;
@@ -1167,6 +1216,12 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&cb.sempty[sr]));
         if (++sr == kSRing) sr = 0;
+        // every accumulator of the stage in flight at once, one wait (a
+        // wait per accumulator costs a tensor-memory round trip each)
+        uint32_t d[kAccs][16];
+#pragma unroll
+        for (int j = 0; j < kAccs; ++j) tmem_ld16(dt + j * 16, d[j]);
+        tmem_wait_ld();
 #pragma unroll
         for (int g = 0; g < gps; ++g) {
           // 256 * D_hi + D_lo' summed over the group's accumulators
@@ -1175,11 +1230,9 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
           for (int n = 0; n < kFBM; ++n) tsum[n] = 0;
 #pragma unroll
           for (int j = 0; j < subs; ++j) {
-            uint32_t d[16];
-            tmem_ld16(dt + (g * subs + j) * 16, d);
-            tmem_wait_ld();
 #pragma unroll
-            for (int n = 0; n < kFBM; ++n) tsum[n] += 256 * static_cast<int>(d[n]) + static_cast<int>(d[8 + n]);
+            for (int n = 0; n < kFBM; ++n)
+              tsum[n] += 256 * static_cast<int>(d[g * subs + j][n]) + static_cast<int>(d[g * subs + j][8 + n]);
           }
           const float sc = scs[g];
           const int z = zs[g];
@@ -1197,10 +1250,10 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&cb.dempty[ts]));
-        if (++ts == kTS) {
-          ts = 0;
-          tph ^= 1u;
+        if (lane == 0) mbar_arrive(smem_u32(&cb.dempty[td]));
+        if (++td == C::dslots) {
+          td = 0;
+          dph ^= 1u;
         }
       }
       const int* cols = e + 4;
@@ -1243,10 +1296,11 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 // ---------------------------------------------------------------------------
 template <int SK, int G>
 __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
-  constexpr int kTS = StageCfg<SK>::tslots, kAccs = StageCfg<SK>::accs;
+  using C = StageCfg<SK>;
+  constexpr int kAccs = C::accs;
   static_assert(SK / G >= 1 && SK / G <= kAccs && kAccs % (SK / G) == 0, "a stage's groups share the accumulators");
-  static_assert(SK / G <= kMaxStageGroups && kTS <= kMaxTSlots, "stage groups and slots fit the control blocks");
-  static_assert(kTS * (SK / 4 + kAccs * 16 + 2 * kQCols) <= kTmemCols, "tensor-memory ring fits 512 columns");
+  static_assert(SK / G <= kMaxStageGroups && C::aslots <= kMaxASlots && C::dslots <= kMaxDSlots && C::dslots >= 2, "slots");
+  static_assert(C::dbase + C::dslots * C::dstride <= kTmemCols, "rings fit");
   extern __shared__ __align__(128) uint8_t smem[];
   Ctrl& cb = *reinterpret_cast<Ctrl*>(smem);
   int* table = reinterpret_cast<int*>(smem + kCtrlBytes);
@@ -1265,8 +1319,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
       mbar_init(smem_u32(&cb.xempty[i]), kMmaIssuers + 4);
       mbar_init(smem_u32(&cb.qfull[i]), 1);
     }
-    for (int i = 0; i < kTS; ++i) {
+    for (int i = 0; i < C::aslots; ++i) {
       mbar_init(smem_u32(&cb.afull[i]), kDQ);
+      mbar_init(smem_u32(&cb.aempty[i]), 1);
+    }
+    for (int i = 0; i < C::dslots; ++i) {
       mbar_init(smem_u32(&cb.dfull[i]), 1);
       mbar_init(smem_u32(&cb.dempty[i]), 4);
     }
@@ -1354,6 +1411,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     *reinterpret_cast<uint2*>(a.out + o) = packed;
     if (a.out_f32) *reinterpret_cast<float4*>(a.out_f32 + o) = sum;
   }
+  finish_call(a, &cb.last);
 }
 
 // ---------------------------------------------------------------------------
@@ -1420,8 +1478,9 @@ bool fused_supported(int H, int I, int G) {
   if (f.sk % G) return false;
   // tensor memory: slots x (A tile + accumulators) <= 512 columns; every
   // group of a stage gets a whole number of the stage's accumulators
-  const int ts = tslots_for(f.sk), acc = accs_for(f.sk);
-  if (ts * (f.sk / 4 + acc * 16 + 2 * kQCols) > kTmemCols) return false;
+  const int acc = accs_for(f.sk);
+  if (aslots_for(f.sk) * (f.sk / 4) + dslots_for(f.sk) * dslot_cols(f.sk) > kTmemCols || dslots_for(f.sk) < 2)
+    return false;
   if (f.sk / G > acc || acc % (f.sk / G) || (G / 32) % (acc / (f.sk / G))) return false;
   return f.stages >= kMinStages;
 }
@@ -1442,8 +1501,21 @@ static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream
       return MTP_ERR_CUDA;
     configured = dev;
   }
-  moe_fused_kernel<SK, G><<<device_sms(), kThreads, f.smem, st>>>(a);
-  return launch_status();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(device_sms()));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = f.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, moe_fused_kernel<SK, G>, a) != cudaSuccess) {
+    cudaGetLastError();
+    return MTP_ERR_LAUNCH;
+  }
+  return MTP_OK;
 }
 
 int launch_moe_fused(const FusedArgs& a_in, cudaStream_t st) {

@@ -36,6 +36,26 @@ def cuda_device(built_lib):
     return torch.device("cuda:0")
 
 
+_PARITY = []
+
+
+def record_parity(**fields):
+    """Parity figures of one check, with the test that made it; written to the
+    JSON file named by MTP_PARITY_LOG (if set) when the session ends."""
+    import os
+    fields["test"] = os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0]
+    _PARITY.append(fields)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    import json
+    import os
+    path = os.environ.get("MTP_PARITY_LOG")
+    if path and _PARITY:
+        with open(path, "w") as f:
+            json.dump(_PARITY, f, indent=1)
+
+
 def golden(name: str):
     import torch
     return torch.load(GOLDEN / name, weights_only=False)

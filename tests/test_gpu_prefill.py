@@ -71,28 +71,71 @@ def test_prefill_given_ids_with_skipped_pairs_and_sym8(cuda_device):
     check(out, ref)
 
 
-def test_prefill_config4_shape_matches_decode_kernel(cuda_device):
-    """Config-4 layer shape (E = 256, H = 2048, I = 512, top-8, shared expert)
-    at M = 2048 through the router: the prefill path against the decode kernel
-    (itself checked against the oracle), plus oracle rows; repeated calls are
-    bit-identical."""
+def test_prefill_config4_matches_oracle_and_decode_kernel(cuda_device):
+    """BASELINE config 4's layer (E = 256, H = 2048, I = 512, top-8, shared
+    expert) at its own size, M = 8192, through the router: 64 strided rows
+    against the fp32 oracle, every row against the decode kernel (itself
+    checked against the oracle), and repeated calls bit-identical."""
     import mtp_b200
     from mtp_b200.synthetic import CONFIG1, make_inputs, make_layer
+    m = 8192
     experts, sh = make_layer(CONFIG1, seed=0, device=cuda_device)
     w, s = build(experts, sh, cuda_device)
-    x, logits = make_inputs(CONFIG1, 2048, seed=5, device=cuda_device)
+    x, logits = make_inputs(CONFIG1, m, seed=5, device=cuda_device)
     a = mtp_b200.moe_layer_w4a16(x, logits, w, 8, shared=s, path="prefill")
     b = mtp_b200.moe_layer_w4a16(x, logits, w, 8, shared=s, path="prefill")
     assert torch.equal(a, b)
     dec = mtp_b200.moe_layer_w4a16(x, logits, w, 8, shared=s, path="decode")
     check(a, dec.float().cpu())
     ow, oids, _ = orouter.topk_softmax(logits.cpu().numpy(), 8, True)
-    rows = [0, 1, 777, 2047]
+    rows = np.linspace(0, m - 1, num=64).astype(int).tolist()
     need = sorted({int(v) for r in rows for v in oids[r]})
     cpu_ex = {kk: {ee: experts[kk][ee].cpu() for ee in need} for kk in KEYS}
     o = olayer.MoeLayerOracle(cpu_ex, {kk: v.cpu() for kk, v in sh.items()})
     ref = o.moe_tokens(x[rows].float().cpu(), torch.as_tensor(oids[rows]), torch.as_tensor(ow[rows]))
     check(a[rows], ref)
+    check(dec[rows], ref)
+
+
+@pytest.mark.parametrize("e,h,i,k,m,shared", [
+    (8, 256, 128, 2, 300, True),        # partial blocks, the shared expert as expert E
+    (256, 2048, 512, 8, 8192, True),    # config 4
+    (16, 512, 256, 4, 700, False),      # no shared expert
+])
+def test_prefill_align_tables_match_oracle(cuda_device, e, h, i, k, m, shared):
+    """The prefill path's own align (histogram, offsets, stable scatter in
+    three launches) against the moe_align_block_size restatement, bit for
+    bit: the pairs extended by the shared expert (expert E), then sorted pair
+    indices (valid region), expert of every used block and
+    num_tokens_post_padded, at block size 128 with pad_sorted_ids."""
+    import mtp_b200
+    from mtp_b200 import _lib
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    from oracle import align as oalign
+    cfg = LayerConfig(num_experts=e, hidden=h, inter=i, top_k=k, shared=shared, tokens=(m,))
+    experts, sh = make_layer(cfg, seed=e + m, device=cuda_device)
+    w, s = build(experts, sh, cuda_device)
+    x, logits = make_inputs(cfg, m, seed=31, device=cuda_device)
+    ws = mtp_b200.prefill_workspace(m, w, k, cuda_device)
+    mtp_b200.moe_layer_w4a16(x, logits, w, k, shared=s, workspace=ws, path="prefill")
+    torch.cuda.synchronize()
+    t = _lib.prefill_tables(m, e, k, h, i, shared)
+    kx = k + (1 if shared else 0)
+    assert t.pairs_per_token == kx and t.block_size == 128
+
+    def view(off, n):
+        return ws[off:off + 4 * n].view(torch.int32).cpu().numpy()
+
+    _, oids, _ = orouter.topk_softmax(logits.cpu().numpy(), k, True)
+    ids_x = np.concatenate([oids, np.full((m, 1), e, np.int32)], axis=1) if shared else oids
+    assert np.array_equal(view(t.pair_expert_ids, m * kx).reshape(m, kx), ids_x)
+    ref_sorted, ref_eids, ref_ntpp, _ = oalign.moe_align_block_size(ids_x, 128, e + (1 if shared else 0),
+                                                                     pad_sorted_ids=True)
+    ntpp = int(view(t.num_tokens_post_padded, 1)[0])
+    assert ntpp == int(ref_ntpp[0])
+    assert t.capacity >= ntpp and t.capacity == ref_sorted.size
+    assert np.array_equal(view(t.sorted_token_ids, ntpp), ref_sorted[:ntpp])
+    assert np.array_equal(view(t.expert_ids, ntpp // 128), ref_eids[:ntpp // 128])
 
 
 def test_auto_path_choice(cuda_device):
