@@ -298,6 +298,9 @@ typedef struct MtpPrefetchConfig {
   uint8_t* cache_base;             /* device [num_layers][slots][bytes]        */
   int32_t* slot_tables;            /* device [num_layers][num_experts], set to -1 */
   int32_t simulate;
+  int64_t host_layer_stride;       /* bytes between layers in host_store:
+                                      0 = num_experts * expert_bytes, -1 = all
+                                      layers share one [experts][bytes] block */
 } MtpPrefetchConfig;
 
 typedef struct MtpPrefetchStats {  /* CacheManagerSnapshot counters (cache_manager.py:193-205) */
@@ -327,6 +330,14 @@ MTP_API int mtp_prefetch_layer_used(uint64_t handle, int32_t layer, void* comput
  * needs the copy complete now. insert_on_miss copies missing experts in.    */
 MTP_API int mtp_prefetch_demand(uint64_t handle, int32_t layer, const int32_t* experts, int32_t count,
                                 int32_t insert_on_miss, int32_t* out_hits);
+/* Make compute_stream wait for the copies still in flight of the given
+ * experts of `layer` (issued ahead or queued by demand), so the layer call
+ * enqueued next reads them from the slot cache instead of fetching the same
+ * bytes from the host store a second time. Non-blocking on the host.
+ * Counterpart of the ready-time wait of ReadyTimeExpertCacheManager.demand
+ * (runtime/cache_manager.py:399), which charges a late copy's remaining time. */
+MTP_API int mtp_prefetch_wait(uint64_t handle, int32_t layer, const int32_t* experts, int32_t count,
+                              void* compute_stream);
 /* Non-blocking: retire completed copies and report the counters.           */
 MTP_API int mtp_prefetch_poll(uint64_t handle, MtpPrefetchStats* out);
 MTP_API int mtp_prefetch_sync(uint64_t handle);

@@ -39,6 +39,7 @@ EXPORTS = (
     "mtp_prefetch_issue",
     "mtp_prefetch_layer_used",
     "mtp_prefetch_demand",
+    "mtp_prefetch_wait",
     "mtp_prefetch_poll",
     "mtp_prefetch_sync",
 )
@@ -77,7 +78,7 @@ class MtpPrefillTables(C.Structure):
 class MtpPrefetchConfig(C.Structure):
     _fields_ = [("device", i32), ("num_layers", i32), ("num_experts", i32), ("slots_per_layer", i32),
                 ("expert_bytes", i64), ("host_store", vp), ("cache_base", vp), ("slot_tables", vp),
-                ("simulate", i32)]
+                ("simulate", i32), ("host_layer_stride", i64)]
 
 
 class MtpPrefetchStats(C.Structure):
@@ -114,6 +115,7 @@ _SIGS = {
     "mtp_prefetch_issue": (C.c_int, [u64, i32, vp, i32, C.POINTER(i32)]),
     "mtp_prefetch_layer_used": (C.c_int, [u64, i32, vp]),
     "mtp_prefetch_demand": (C.c_int, [u64, i32, vp, i32, i32, C.POINTER(i32)]),
+    "mtp_prefetch_wait": (C.c_int, [u64, i32, vp, i32, vp]),
     "mtp_prefetch_poll": (C.c_int, [u64, C.POINTER(MtpPrefetchStats)]),
     "mtp_prefetch_sync": (C.c_int, [u64]),
 }

@@ -136,8 +136,13 @@ int fill(Session* s, int l, int e, bool prefetched) {
   int32_t* table = s->cfg.slot_tables + static_cast<int64_t>(l) * E;
   if (old >= 0) set_entry_kernel<<<1, 1, 0, st>>>(table, old, -1);
   const int64_t eb = s->cfg.expert_bytes;
+  // host_layer_stride: 0 = one [experts][bytes] block per layer, -1 = every
+  // layer reads the same block, > 0 = that many bytes between layers
+  const int64_t hstride = s->cfg.host_layer_stride == 0 ? static_cast<int64_t>(E) * eb
+                                                        : (s->cfg.host_layer_stride < 0 ? 0 : s->cfg.host_layer_stride);
   if (cudaMemcpyAsync(s->cfg.cache_base + (static_cast<int64_t>(l) * S + v) * eb,
-                      s->cfg.host_store + (static_cast<int64_t>(l) * E + e) * eb, static_cast<size_t>(eb),
+                      s->cfg.host_store + static_cast<int64_t>(l) * hstride + static_cast<int64_t>(e) * eb,
+                      static_cast<size_t>(eb),
                       cudaMemcpyHostToDevice, st) != cudaSuccess)
     return MTP_ERR_CUDA;
   set_entry_kernel<<<1, 1, 0, st>>>(table, e, v);
@@ -172,6 +177,7 @@ int mtp_prefetch_session_create(const MtpPrefetchConfig* cfg, uint64_t* out_hand
       cfg->num_layers > 4096 || cfg->num_experts > 4096 || cfg->slots_per_layer > cfg->num_experts)
     return MTP_ERR_SHAPE;
   if (!cfg->simulate && (!cfg->host_store || !cfg->cache_base || !cfg->slot_tables)) return MTP_ERR_NULL;
+  if (cfg->host_layer_stride < -1) return MTP_ERR_SHAPE;
   auto* s = new Session();
   s->cfg = *cfg;
   std::memset(&s->st, 0, sizeof(s->st));
@@ -304,6 +310,29 @@ int mtp_prefetch_demand(uint64_t handle, int32_t layer, const int32_t* experts, 
     }
   }
   if (out_hits) *out_hits = hits;
+  return MTP_OK;
+}
+
+int mtp_prefetch_wait(uint64_t handle, int32_t layer, const int32_t* experts, int32_t count, void* compute_stream) {
+  Session* s = get(handle);
+  if (!s) return MTP_ERR_HANDLE;
+  if (layer < 0 || layer >= s->cfg.num_layers || count < 0) return MTP_ERR_SHAPE;
+  if (count > 0 && !experts) return MTP_ERR_NULL;
+  if (sim(s)) return MTP_OK;
+  if (set_device(s) != MTP_OK) return MTP_ERR_CUDA;
+  Layer& L = s->layers[layer];
+  const cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
+  for (int i = 0; i < count; ++i) {
+    const int e = experts[i];
+    if (e < 0 || e >= s->cfg.num_experts) return MTP_ERR_ARG;
+    const int slot = L.slot_of[e];
+    if (slot < 0) continue;
+    refresh(s, L, slot);
+    if (!L.slots[slot].inflight) continue;
+    if (cudaStreamWaitEvent(cs, s->events[static_cast<size_t>(layer) * s->cfg.slots_per_layer + slot], 0) !=
+        cudaSuccess)
+      return MTP_ERR_CUDA;
+  }
   return MTP_OK;
 }
 

@@ -9,19 +9,32 @@ which is the ``expert_map`` convention of the kernels this path replaces
 tracing/vllm_wna16_group_plan.py:87-95, and reads the EP map at
 tracing/vllm_router_trace.py:7661-7689). Each rank routes its own tokens, then
 
-1. dispatch: every token row goes once to each rank that owns at least one of
-   its experts (rows deduplicated per destination), with its k local ids and
-   weights (weight 0 and id -1 for pairs owned elsewhere);
-2. local compute: the fused layer kernel on the received rows, given the
-   ids and weights (no router, no shared expert): each received row becomes
-   the weighted sum over its local experts;
-3. combine: the partial rows go back to their home rank, which adds them in
-   fp32 to its shared-expert output and rounds once to bf16.
+Two exchange forms:
 
-The exchange runs on ``torch.distributed`` ``all_to_all_single`` (NCCL over
-NVLink on the GPU, gloo in the CPU tests). Row payloads travel as bf16 bits
-in int32 views (two values per word; H is even), the id / weight lists as one
-int32 tensor. The decode configs do not shard: they run one replica per GPU.
+* ``tokens_per_rank`` given (every rank holds the same number of tokens, as a
+  prefill chunk does): no host synchronisation and fixed message sizes.
+  1. all-gather the token rows and their (id, weight) lists;
+  2. the layer kernel on every gathered row with the ids of other ranks'
+     experts set to -1, writing fp32 partial rows;
+  3. reduce-scatter (sum) of the fp32 partials back to the home ranks, which
+     add their tokens' gated shared-expert output and round once to bf16.
+  The bytes moved equal those of an all-to-all padded to the per-rank
+  capacity a fixed-size exchange needs (a token may use every rank).
+* otherwise (ranks with different token counts): a deduplicated all-to-all.
+  1. dispatch: every token row goes once to each rank that owns at least one
+     of its experts, with its k local ids and weights (weight 0 and id -1 for
+     pairs owned elsewhere); the split sizes are exchanged first (host syncs);
+  2. local compute: the layer kernel on the received rows (no router, no
+     shared expert), each row becoming the weighted sum over its local
+     experts, rounded to bf16 for the return trip;
+  3. combine: the partial rows go back to their home rank, which adds them in
+     fp32 to its shared-expert output and rounds once to bf16 (one more bf16
+     rounding per remote rank than the single-device layer).
+
+The exchanges run on ``torch.distributed`` (NCCL over NVLink on the GPU, gloo
+in the CPU tests). Row payloads travel as bf16 bits in int32 views (two values
+per word; H is even), the id / weight lists as one int32 tensor. The decode
+configs do not shard: they run one replica per GPU.
 """
 from __future__ import annotations
 
@@ -87,6 +100,29 @@ def _all_to_all(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
 
 
+def _all_gather(out: torch.Tensor, inp: torch.Tensor, group, world: int):
+    """Rank-ordered concatenation along dim 0 (NCCL all_gather_into_tensor;
+    the list form on backends without it)."""
+    if world == 1:
+        out.copy_(inp)
+    elif inp.device.type == "cuda":
+        dist.all_gather_into_tensor(out, inp, group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), inp, group=group)
+
+
+def _reduce_scatter_sum(out: torch.Tensor, inp: torch.Tensor, group, world: int):
+    """out = sum over ranks of this rank's dim-0 chunk of inp (NCCL
+    reduce_scatter_tensor; all_reduce then slice on backends without it)."""
+    if world == 1:
+        out.copy_(inp)
+    elif inp.device.type == "cuda":
+        dist.reduce_scatter_tensor(out, inp, group=group)
+    else:
+        dist.all_reduce(inp, group=group)
+        out.copy_(inp.chunk(world)[dist.get_rank(group)])
+
+
 def _exchange_counts(counts: list[int], device, group, world: int) -> list[int]:
     if world == 1:
         return list(counts)
@@ -99,19 +135,22 @@ def _exchange_counts(counts: list[int], device, group, world: int) -> list[int]:
 class ExpertParallelMoE:
     """One expert-parallel MoE layer on this rank.
 
-    ``local_fn(rows, ids, weights)`` computes the received rows: bf16 [R, H],
-    int32 [R, k] local ids (-1 = skip), fp32 [R, k] weights -> bf16 [R, H].
+    ``local_fn(rows, ids, weights, f32=False)`` computes the received rows:
+    bf16 [R, H], int32 [R, k] local ids (-1 = skip), fp32 [R, k] weights ->
+    [R, H] (bf16, or fp32 with ``f32=True``).
     ``router_fn(logits, k)`` returns (weights fp32 [M, k], ids int32 [M, k]),
     ``shared_fn(x)`` the gated shared-expert output bf16 [M, H] (or None).
     :meth:`for_gpu` wires them to the CUDA kernels; the tests inject CPU
     versions to check the exchange on gloo ranks. Without an initialised
     process group (or in a group of one) the layer runs as a single rank that
     owns every expert; ``single_fn(x, logits)``, when given, then computes the
-    whole layer in one call (no dispatch bookkeeping)."""
+    whole layer in one call (no dispatch bookkeeping). With ``tokens_per_rank``
+    every call must bring exactly that many tokens and the exchange is the
+    all-gather / reduce-scatter form (no host synchronisation)."""
 
     def __init__(self, num_experts: int, top_k: int, hidden: int, local_fn: Callable,
                  router_fn: Callable, shared_fn: Callable | None = None, group=None,
-                 single_fn: Callable | None = None):
+                 single_fn: Callable | None = None, tokens_per_rank: int | None = None):
         self.world, self.rank = _world(group)
         self.num_experts = num_experts
         self.epr = experts_per_rank(num_experts, self.world)
@@ -122,10 +161,11 @@ class ExpertParallelMoE:
         self.shared_fn = shared_fn
         self.group = group
         self.single_fn = single_fn
+        self.tokens_per_rank = tokens_per_rank
 
     @classmethod
     def for_gpu(cls, local_experts, num_experts: int, top_k: int, shared=None, renormalize: bool = True,
-                group=None, zero_mode: str = "raw") -> "ExpertParallelMoE":
+                group=None, zero_mode: str = "raw", tokens_per_rank: int | None = None) -> "ExpertParallelMoE":
         """``local_experts``: this rank's shard (``W4A16Experts.shard``)."""
         from . import _lib
         from .ops import layer_path, layer_workspace, moe_layer_w4a16, prefill_workspace, topk_softmax
@@ -145,11 +185,14 @@ class ExpertParallelMoE:
                 cache[path] = ws = make(m, local_experts, top_k, dev)
             return ws
 
-        def local_fn(rows, ids, weights):
+        def local_fn(rows, ids, weights, f32=False):
             m = rows.shape[0]
             path = layer_path(m, local_experts.num_experts, top_k)
-            return moe_layer_w4a16(rows, None, local_experts, top_k, topk_weights=weights, topk_ids=ids,
-                                   zero_mode=zero_mode, workspace=workspace(m, rows.device, path), path=path)
+            out32 = torch.empty((m, rows.shape[1]), dtype=torch.float32, device=rows.device) if f32 else None
+            out = moe_layer_w4a16(rows, None, local_experts, top_k, topk_weights=weights, topk_ids=ids,
+                                  zero_mode=zero_mode, workspace=workspace(m, rows.device, path), path=path,
+                                  out_f32=out32)
+            return out32 if f32 else out
 
         def router_fn(logits, k):
             w, ids, _ = topk_softmax(logits, k, renormalize)
@@ -173,7 +216,8 @@ class ExpertParallelMoE:
             return moe_layer_w4a16(x, logits, local_experts, top_k, renormalize, shared=shared, zero_mode=zero_mode,
                                    workspace=workspace(m, x.device, path), path=path)
 
-        return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group, single_fn)
+        return cls(num_experts, top_k, local_experts.hidden, local_fn, router_fn, shared_fn, group, single_fn,
+                   tokens_per_rank)
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x bf16 [M, H] and router_logits fp32 [M, E] of this rank's tokens -> bf16 [M, H]."""
@@ -186,6 +230,10 @@ class ExpertParallelMoE:
         if self.world == 1 and self.single_fn is not None and m > 0:
             return self.single_fn(x, router_logits)
         weights, ids = self.router_fn(router_logits, k)
+        if self.tokens_per_rank is not None:
+            if m != self.tokens_per_rank:
+                raise ValueError(f"this layer exchanges {self.tokens_per_rank} tokens per rank, got {m}")
+            return self._forward_gathered(x, ids, weights)
         plan = plan_dispatch(ids, weights, self.num_experts, self.world)
         recv_counts = _exchange_counts(plan.counts, dev, self.group, self.world)
         r = sum(recv_counts)
@@ -209,6 +257,28 @@ class ExpertParallelMoE:
         if self.shared_fn is not None and m > 0:
             acc += self.shared_fn(x).float()
         acc.index_add_(0, plan.tokens, back.view(torch.bfloat16).float())
+        return acc.to(torch.bfloat16)
+
+    def _forward_gathered(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+        """All-gather rows and lists, local experts on every row (foreign ids
+        -1), reduce-scatter of the fp32 partials, shared expert at home."""
+        m, h, k, n = x.shape[0], self.hidden, self.top_k, self.world
+        dev = x.device
+        rows = torch.empty((n * m, h // 2), dtype=torch.int32, device=dev)
+        _all_gather(rows, x.contiguous().view(torch.int32), self.group, n)
+        meta = torch.cat([ids.to(torch.int32), weights.float().contiguous().view(torch.int32)], dim=1)
+        all_meta = torch.empty((n * m, 2 * k), dtype=torch.int32, device=dev)
+        _all_gather(all_meta, meta, self.group, n)
+        lo = self.rank * self.epr
+        gid = all_meta[:, :k]
+        mine = (gid >= lo) & (gid < lo + self.epr)
+        lids = torch.where(mine, gid - lo, torch.full_like(gid, -1)).contiguous()
+        lw = torch.where(mine, all_meta[:, k:].view(torch.float32), torch.zeros((), device=dev)).contiguous()
+        part = self.local_fn(rows.view(torch.bfloat16), lids, lw, f32=True).float().contiguous()
+        acc = torch.empty((m, h), dtype=torch.float32, device=dev)
+        _reduce_scatter_sum(acc, part, self.group, n)
+        if self.shared_fn is not None:
+            acc += self.shared_fn(x).float()
         return acc.to(torch.bfloat16)
 
     __call__ = forward

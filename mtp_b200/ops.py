@@ -432,7 +432,8 @@ class PrefetchSession:
     (or None with ``simulate=True``, bookkeeping only)."""
 
     def __init__(self, num_layers: int, num_experts: int, slots_per_layer: int, expert_bytes: int,
-                 host_store: torch.Tensor | None = None, device=None, simulate: bool = False):
+                 host_store: torch.Tensor | None = None, device=None, simulate: bool = False,
+                 shared_host_layers: bool = False):
         import numpy as np  # noqa: F401  (host arrays below)
         self.num_layers, self.num_experts, self.slots = num_layers, num_experts, slots_per_layer
         self.expert_bytes = expert_bytes
@@ -443,17 +444,21 @@ class PrefetchSession:
         else:
             if host_store is None or not host_store.is_pinned():
                 raise ValueError("host_store must be a pinned host tensor")
-            if host_store.numel() != num_layers * num_experts * expert_bytes:
-                raise ValueError("host_store must be [layers, experts, expert_bytes] bytes")
+            want = (1 if shared_host_layers else num_layers) * num_experts * expert_bytes
+            if host_store.numel() != want:
+                raise ValueError("host_store must be [layers, experts, expert_bytes] bytes "
+                                 "([experts, expert_bytes] with shared_host_layers)")
             device = torch.device(device)
             dev_index = device.index if device.index is not None else torch.cuda.current_device()
             # 256-byte aligned slots: expert_bytes is a multiple of 256 (expert layout)
             self.cache = torch.empty(num_layers * slots_per_layer * expert_bytes, dtype=torch.uint8, device=device)
             self.slot_tables = torch.empty(num_layers, num_experts, dtype=torch.int32, device=device)
+        self.shared_host_layers = shared_host_layers
         cfg = _lib.MtpPrefetchConfig(dev_index, num_layers, num_experts, slots_per_layer, expert_bytes,
                                      None if simulate else host_store.data_ptr(),
                                      None if simulate else self.cache.data_ptr(),
-                                     None if simulate else self.slot_tables.data_ptr(), int(simulate))
+                                     None if simulate else self.slot_tables.data_ptr(), int(simulate),
+                                     -1 if shared_host_layers else 0)
         h = _lib.u64()
         _lib.call("mtp_prefetch_session_create", C.byref(cfg), C.byref(h))
         self.handle = h.value
@@ -476,6 +481,12 @@ class PrefetchSession:
         _lib.call("mtp_prefetch_demand", self.handle, layer, p, a.size, int(insert_on_miss), C.byref(out))
         return out.value
 
+    def wait(self, layer: int, experts, stream: torch.cuda.Stream | None = None):
+        """Make ``stream`` wait for the in-flight copies of these experts."""
+        a, p = self._ids(experts)
+        st = stream if stream is not None else torch.cuda.current_stream()
+        _lib.call("mtp_prefetch_wait", self.handle, layer, p, a.size, C.c_void_p(st.cuda_stream))
+
     def layer_used(self, layer: int, stream: torch.cuda.Stream | None = None):
         st = stream if stream is not None else torch.cuda.current_stream()
         _lib.call("mtp_prefetch_layer_used", self.handle, layer, C.c_void_p(st.cuda_stream))
@@ -491,7 +502,7 @@ class PrefetchSession:
     def layer_views(self, layer: int):
         """(expert_blobs, slot_table, host_blobs) of one layer, for moe_layer_w4a16."""
         s0 = layer * self.slots * self.expert_bytes
-        e0 = layer * self.num_experts * self.expert_bytes
+        e0 = 0 if self.shared_host_layers else layer * self.num_experts * self.expert_bytes
         return (self.cache[s0:s0 + self.slots * self.expert_bytes], self.slot_tables[layer],
                 self.host_store.reshape(-1)[e0:e0 + self.num_experts * self.expert_bytes])
 

@@ -58,7 +58,7 @@ def cpu_rank(rank: int, world: int, port: int, cfg: dict, queue):
             lo = cfg["skip_rank"] * epr
             logits[:, lo:lo + epr] = -1e4
 
-        def local_fn(rows, ids, w):
+        def local_fn(rows, ids, w, f32=False):
             out = torch.zeros(rows.shape, dtype=torch.float32)
             xf = rows.float()
             for r in range(rows.shape[0]):
@@ -66,7 +66,7 @@ def cpu_rank(rank: int, world: int, port: int, cfg: dict, queue):
                     e = int(ids[r, j])
                     if e >= 0:
                         out[r] += float(w[r, j]) * olayer.expert_mlp(xf[r:r + 1], *dq[rank * epr + e])[0]
-            return out.to(torch.bfloat16)
+            return out if f32 else out.to(torch.bfloat16)
 
         def router_fn(lg, k):
             w, ids, _ = orouter.topk_softmax(lg.numpy(), k, True)
@@ -81,7 +81,8 @@ def cpu_rank(rank: int, world: int, port: int, cfg: dict, queue):
                 xf = xx.float()
                 return (torch.sigmoid(F.linear(xf, gw[None]))[:, :1] * olayer.expert_mlp(xf, *sdq)).to(torch.bfloat16)
 
-        layer = ExpertParallelMoE(c.num_experts, c.top_k, c.hidden, local_fn, router_fn, shared_fn)
+        layer = ExpertParallelMoE(c.num_experts, c.top_k, c.hidden, local_fn, router_fn, shared_fn,
+                                  tokens_per_rank=m if cfg.get("gather") else None)
         out = layer(x, logits)
         w, ids, _ = orouter.topk_softmax(logits.numpy(), c.top_k, True)
         if m:
@@ -116,7 +117,8 @@ def gpu_rank(rank: int, world: int, port: int, cfg: dict, queue):
         experts, shared = make_layer(c, seed=5, device=dev)
         full = W4A16Experts.from_gptq(*(experts[kk] for kk in KEYS), group_size=c.group_size)
         sh = SharedExpert.from_gptq(*(shared[kk] for kk in KEYS), shared["gate_weight"], group_size=c.group_size)
-        layer = ExpertParallelMoE.for_gpu(full.shard(rank, world), c.num_experts, c.top_k, shared=sh)
+        layer = ExpertParallelMoE.for_gpu(full.shard(rank, world), c.num_experts, c.top_k, shared=sh,
+                                          tokens_per_rank=cfg["M"] if cfg.get("gather") else None)
         x, logits = make_inputs(c, cfg["M"], seed=200 + rank, device=dev)
         out = layer(x, logits)
         ref = mtp_b200.moe_layer_w4a16(x, logits, full, c.top_k, shared=sh)

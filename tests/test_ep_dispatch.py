@@ -62,6 +62,10 @@ def test_plan_dispatch_rejects_uneven_shards():
     (2, dict(E=8, H=256, I=128, k=2, G=128, shared=True, M=[6, 5])),
     (4, dict(E=16, H=256, I=128, k=4, G=64, shared=False, M=[5, 0, 7, 3])),
     (2, dict(E=8, H=256, I=128, k=2, G=128, shared=True, M=[4, 4], skip_rank=1)),
+    # the all-gather / reduce-scatter form (equal tokens per rank)
+    (2, dict(E=8, H=256, I=128, k=2, G=128, shared=True, M=[5, 5], gather=True)),
+    (4, dict(E=16, H=256, I=128, k=4, G=64, shared=False, M=[3, 3, 3, 3], gather=True)),
+    (2, dict(E=8, H=256, I=128, k=2, G=128, shared=True, M=[4, 4], skip_rank=0, gather=True)),
 ])
 def test_ep_round_trip_on_gloo_ranks_matches_single_device(world, cfg):
     res = _run(ep_workers.cpu_rank, world, cfg)
@@ -72,10 +76,11 @@ def test_ep_round_trip_on_gloo_ranks_matches_single_device(world, cfg):
 
 
 @pytest.mark.gpu
-def test_ep_round_trip_on_two_gpus_matches_single_gpu_layer():
+@pytest.mark.parametrize("gather", [False, True])
+def test_ep_round_trip_on_two_gpus_matches_single_gpu_layer(gather):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    cfg = dict(E=256, H=2048, I=512, k=8, G=128, M=512)
+    cfg = dict(E=256, H=2048, I=512, k=8, G=128, M=512, gather=gather)
     res = _run(ep_workers.gpu_rank, 2, cfg, timeout=600.0)
     for rank, (r, err) in res.items():
         assert err is None, f"rank {rank}: {err}"
