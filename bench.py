@@ -744,8 +744,46 @@ def run_predictor(dev, hbm_gbs):
         rows.append({"M": m, "us": round(us, 2), "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm_gbs, 4),
                      "launches_per_call": 3})
         del g
+    # the reference's own architecture at its default size (hidden 2048,
+    # width 256, 40 layers, 4 deltas, 256 experts; random weights)
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    rnd = lambda *shape, s=0.02: (torch.randn(*shape, generator=gen) * s).to(torch.bfloat16).to(dev)
+    hr = [mtp_b200.HiddenResidualPredictor(rnd(256, 2048), rnd(256), 1.0 + rnd(256), rnd(256), rnd(40, 256, s=1.0),
+                                           rnd(4, 256, s=1.0), rnd(256, 256), rnd(256)) for _ in range(copies)]
+    hr_bytes = 2 * (256 * 2048 + 256 * 256 + 40 * 256 + 4 * 256 + 4 * 256)
+    hr_rows = []
+    for m in cfg.tokens:
+        h = make_predictor_inputs(cfg, m, seed=m).to(dev)
+        lids = torch.arange(m, dtype=torch.int32, device=dev) % 40
+        ws = hr[0].workspace(m, dev)
+        ids = torch.empty(m, 4, cfg.top_k, dtype=torch.int32, device=dev)
+
+        def hcalls():
+            for p in hr:
+                p.predict_topk(h, lids, cfg.top_k, ids_out=ids, workspace=ws)
+
+        hcalls()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            hcalls()
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (10 * copies)
+        hr_rows.append({"M": m, "us": round(us, 2), "launches_per_call": 4})
+        del g
     return {"config": "config3 predictor 2048->2048->4x256 bf16, top-8 per future layer; 12 weight copies "
-                      "(151 MB > L2) per CUDA graph", "weight_bytes": wbytes, "sweep": rows}
+                      "(151 MB > L2) per CUDA graph", "weight_bytes": wbytes, "sweep": rows,
+            "hidden_residual": {"config": "reference HiddenResidualExpertPredictor shape: hidden 2048 -> width 256 "
+                                          "-> LayerNorm + layer/delta embeddings -> classifier 256 experts, 4 deltas, "
+                                          "top-8; 12 weight copies per CUDA graph (weights fit L2: latency-bound)",
+                                "weight_bytes": hr_bytes, "sweep": hr_rows}}
 
 
 def run_e2e(args, layers, cfg, sweep, dev, state):
@@ -864,6 +902,7 @@ def main():
         # reduction to gain), and a rank that dies while bound to an NVLink
         # multicast object can fault its peers' GPUs.
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     res = run_gpu(args, rank, world)
     if rank == 0 and world == 1 and not args.no_cpu:

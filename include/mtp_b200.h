@@ -273,6 +273,30 @@ MTP_API int mtp_predict_topk(const uint16_t* h, int32_t M, int32_t hidden, const
                              float* logits_out, int32_t* ids_out, void* workspace,
                              int64_t workspace_bytes, void* stream);
 
+/* The reference predictor architecture, HiddenResidualExpertPredictor.forward
+ * (training/hidden_residual.py:44-103): state = LayerNorm(silu(W1 . h + b1))
+ * (ln_weight, ln_bias may be NULL = 1 / 0; biased variance; ln_eps), then for
+ * every future delta f < future the shared classifier
+ * logits[m, f] = Wc . silu(state + layer_emb[layer_ids[m]] + delta_emb[f]) + bc
+ * and the top_k experts of each (m, f) into ids_out [M, future, top_k]
+ * (logits_out [M, future, experts] fp32 optional). W1 [width, hidden] and
+ * Wc [experts, width] bf16 are packed by mtp_predictor_pack; b1 [width],
+ * ln_weight / ln_bias [width], layer_emb [num_layers, width], delta_emb
+ * [future, width], bc [experts] bf16; layer_ids [M] int32 (NULL = layer 0;
+ * clamped to the table). The classifier's input columns are rounded to bf16.
+ * Workspace: mtp_predictor_hr_workspace_size bytes.                         */
+MTP_API int mtp_predictor_hr_workspace_size(int32_t M, int32_t width, int32_t future, int32_t experts,
+                                            int64_t* bytes);
+MTP_API int mtp_predict_topk_hidden_residual(const uint16_t* h, const int32_t* layer_ids, int32_t M,
+                                             int32_t hidden, const uint16_t* w1_packed, const uint16_t* b1,
+                                             int32_t width, const uint16_t* ln_weight,
+                                             const uint16_t* ln_bias, float ln_eps,
+                                             const uint16_t* layer_emb, int32_t num_layers,
+                                             const uint16_t* delta_emb, int32_t future,
+                                             const uint16_t* wc_packed, const uint16_t* bc, int32_t experts,
+                                             int32_t top_k, float* logits_out, int32_t* ids_out,
+                                             void* workspace, int64_t workspace_bytes, void* stream);
+
 
 /* ---- expert prefetch session (premap slot cache) ----------------------------
  * A per-layer HBM slot cache of expert blobs (slots_per_layer of num_experts

@@ -8,11 +8,13 @@ interfaces. There is no CPU fallback.
 from ._lib import MtpError, load as load_library  # noqa: F401
 from .ep import ExpertParallelMoE, plan_dispatch  # noqa: F401
 from .ops import (  # noqa: F401
+    HiddenResidualPredictor,
     MtpPredictor,
     PrefetchSession,
     SharedExpert,
     W4A16Experts,
     dequantize_gptq_projection,
+    experts_from_vllm_wna16,
     fused_experts,
     layer_path,
     layer_workspace,
@@ -20,10 +22,12 @@ from .ops import (  # noqa: F401
     moe_layer_w4a16,
     prefill_workspace,
     topk_softmax,
+    vllm_wna16_to_gptq,
 )
 
 __all__ = [
     "ExpertParallelMoE",
+    "HiddenResidualPredictor",
     "MtpError",
     "MtpPredictor",
     "PrefetchSession",
@@ -31,6 +35,7 @@ __all__ = [
     "SharedExpert",
     "W4A16Experts",
     "dequantize_gptq_projection",
+    "experts_from_vllm_wna16",
     "fused_experts",
     "layer_path",
     "layer_workspace",
@@ -39,4 +44,5 @@ __all__ = [
     "plan_dispatch",
     "prefill_workspace",
     "topk_softmax",
+    "vllm_wna16_to_gptq",
 ]

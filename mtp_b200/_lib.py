@@ -34,6 +34,8 @@ EXPORTS = (
     "mtp_predictor_pack",
     "mtp_predictor_workspace_size",
     "mtp_predict_topk",
+    "mtp_predictor_hr_workspace_size",
+    "mtp_predict_topk_hidden_residual",
     "mtp_prefetch_session_create",
     "mtp_prefetch_session_destroy",
     "mtp_prefetch_issue",
@@ -110,6 +112,9 @@ _SIGS = {
     "mtp_predictor_pack": (C.c_int, [vp, i32, i32, vp, vp]),
     "mtp_predictor_workspace_size": (C.c_int, [i32, i32, i32, i32, C.POINTER(i64)]),
     "mtp_predict_topk": (C.c_int, [vp, i32, i32, vp, vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, i64, vp]),
+    "mtp_predictor_hr_workspace_size": (C.c_int, [i32, i32, i32, i32, C.POINTER(i64)]),
+    "mtp_predict_topk_hidden_residual": (C.c_int, [vp, vp, i32, i32, vp, vp, i32, vp, vp, C.c_float, vp, i32, vp,
+                                                   i32, vp, vp, i32, i32, vp, vp, vp, i64, vp]),
     "mtp_prefetch_session_create": (C.c_int, [C.POINTER(MtpPrefetchConfig), C.POINTER(u64)]),
     "mtp_prefetch_session_destroy": (C.c_int, [u64]),
     "mtp_prefetch_issue": (C.c_int, [u64, i32, vp, i32, C.POINTER(i32)]),

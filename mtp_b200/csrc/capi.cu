@@ -365,7 +365,9 @@ static bool predictor_shapes_ok(int M, int hidden, int width, int future, int ex
 int mtp_predictor_workspace_size(int32_t M, int32_t width, int32_t future, int32_t experts, int64_t* bytes) {
   if (!bytes) return MTP_ERR_NULL;
   if (M < 1 || width < 1 || future < 1 || experts < 1) return MTP_ERR_SHAPE;
-  *bytes = round_up(2LL * M * width, 256) + round_up(4LL * M * future * experts, 256);
+  // fp32 partial sums of both linears, one slice per K-split
+  *bytes = round_up(4LL * kMaxPredictorKs * M * width, 256) +
+           round_up(4LL * kMaxPredictorKs * M * future * experts, 256);
   return MTP_OK;
 }
 
@@ -382,10 +384,44 @@ int mtp_predict_topk(const uint16_t* h, int32_t M, int32_t hidden, const uint16_
   mtp_predictor_workspace_size(M, width, future, experts, &need);
   if (workspace_bytes < need) return MTP_ERR_WORKSPACE;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  uint16_t* hidden2 = reinterpret_cast<uint16_t*>(ws);
-  float* logits = logits_out ? logits_out : reinterpret_cast<float*>(ws + round_up(2LL * M * width, 256));
-  return predictor_run(h, M, hidden, w1_packed, b1, width, w2_packed, b2, future, experts, top_k, logits, ids_out,
-                       hidden2, static_cast<cudaStream_t>(stream));
+  float* part1 = reinterpret_cast<float*>(ws);
+  float* part2 = reinterpret_cast<float*>(ws + round_up(4LL * kMaxPredictorKs * M * width, 256));
+  return predictor_run(h, M, hidden, w1_packed, b1, width, w2_packed, b2, future, experts, top_k, logits_out, ids_out,
+                       part1, part2, static_cast<cudaStream_t>(stream));
+}
+
+int mtp_predictor_hr_workspace_size(int32_t M, int32_t width, int32_t future, int32_t experts, int64_t* bytes) {
+  if (!bytes) return MTP_ERR_NULL;
+  if (M < 1 || width < 1 || future < 1 || experts < 1) return MTP_ERR_SHAPE;
+  *bytes = round_up(4LL * kMaxPredictorKs * M * width, 256) + round_up(2LL * M * future * width, 256) +
+           round_up(4LL * kMaxPredictorKs * M * future * experts, 256);
+  return MTP_OK;
+}
+
+int mtp_predict_topk_hidden_residual(const uint16_t* h, const int32_t* layer_ids, int32_t M, int32_t hidden,
+                                     const uint16_t* w1_packed, const uint16_t* b1, int32_t width,
+                                     const uint16_t* ln_weight, const uint16_t* ln_bias, float ln_eps,
+                                     const uint16_t* layer_emb, int32_t num_layers, const uint16_t* delta_emb,
+                                     int32_t future, const uint16_t* wc_packed, const uint16_t* bc, int32_t experts,
+                                     int32_t top_k, float* logits_out, int32_t* ids_out, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  if (!h || !w1_packed || !wc_packed || !layer_emb || !delta_emb || !ids_out || !workspace) return MTP_ERR_NULL;
+  if (!predictor_shapes_ok(M, hidden, width, future, experts, top_k) || experts % 16 || num_layers < 1 ||
+      !(ln_eps > 0.f))
+    return MTP_ERR_SHAPE;
+  if (!aligned(h, 16) || !aligned(w1_packed, 16) || !aligned(wc_packed, 16) || !aligned(workspace, 256) ||
+      (logits_out && !aligned(logits_out, 4)))
+    return MTP_ERR_ALIGN;
+  int64_t need = 0;
+  mtp_predictor_hr_workspace_size(M, width, future, experts, &need);
+  if (workspace_bytes < need) return MTP_ERR_WORKSPACE;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const int64_t o1 = round_up(4LL * kMaxPredictorKs * M * width, 256);
+  const int64_t o2 = o1 + round_up(2LL * M * future * width, 256);
+  return predictor_hr_run(h, layer_ids, M, hidden, w1_packed, b1, width, ln_weight, ln_bias, ln_eps, layer_emb,
+                          num_layers, delta_emb, future, wc_packed, bc, experts, top_k, logits_out, ids_out,
+                          reinterpret_cast<float*>(ws), reinterpret_cast<uint16_t*>(ws + o1),
+                          reinterpret_cast<float*>(ws + o2), static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -72,9 +72,16 @@ int gptq_dequant(const int32_t* q, const int32_t* z, const uint16_t* s, const in
                  int N, int G, int zero_mode, float* out, cudaStream_t st);
 
 int predictor_pack(const uint16_t* w, int rows, int cols, uint16_t* out, cudaStream_t st);
+// K-splits of the predictor's linears are at most this (workspace sizing).
+constexpr int kMaxPredictorKs = 8;
 int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const uint16_t* b1, int width,
                   const uint16_t* w2p, const uint16_t* b2, int F, int E, int k, float* logits, int32_t* ids,
-                  uint16_t* hidden2, cudaStream_t st);
+                  float* part1, float* part2, cudaStream_t st);
+int predictor_hr_run(const uint16_t* h, const int32_t* layer_ids, int M, int H, const uint16_t* w1p,
+                     const uint16_t* b1, int width, const uint16_t* ln_w, const uint16_t* ln_b, float eps,
+                     const uint16_t* layer_emb, int num_layers, const uint16_t* delta_emb, int F,
+                     const uint16_t* wcp, const uint16_t* bc, int E, int k, float* logits, int32_t* ids, float* part1,
+                     uint16_t* ctx, float* part2, cudaStream_t st);
 
 bool fused_supported(int H, int I, int G);
 int fused_max_work_segments(int M, int max_seg, int max_blocks);

@@ -54,20 +54,27 @@ __global__ void pack_kernel(const uint32_t* __restrict__ w, int rows, int cols, 
   out[i] = w[(static_cast<int64_t>(row) * cols + k) / 2];
 }
 
-// One linear layer: out[m][row] for the CTA's 16 rows, all M columns.
-// mode 0: out_bf16 = bf16(silu(acc + bias)); mode 1: out_f32 = acc + bias.
-__global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restrict__ x, int M, int K,
-                                                         const uint4* __restrict__ wp, const uint16_t* __restrict__ bias,
-                                                         int R, int mode, uint16_t* __restrict__ out_bf16,
-                                                         float* __restrict__ out_f32) {
+// One linear layer's share: CTA (strip, ks) takes the 16 output rows of its
+// strip over K range ks of KS (all M token columns) and writes fp32 partial
+// sums part[ks][m][row] (no bias): KS > 1 spreads the weight stream over more
+// SMs, and the consumer adds the KS slices in a fixed order, so the result
+// does not depend on scheduling. The input is either bf16 rows x [M][K], or
+// (x == NULL) the previous linear's fp32 partials xin[KSin][M][K], finished
+// on load: bf16(silu(sum + xbias)).
+__global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restrict__ x,
+                                                         const float* __restrict__ xin, int KSin,
+                                                         const uint16_t* __restrict__ xbias, int M, int K,
+                                                         const uint4* __restrict__ wp, int R, int KS,
+                                                         float* __restrict__ part) {
   extern __shared__ __align__(16) uint8_t psm[];
-  const int row_stride = 2 * K + 16;  // bf16 row of a token + 16 bytes: conflict-free B fragments
+  // the staged bf16 row holds this CTA's K range only (+ 16 bytes: conflict-free B fragments)
+  const int row_stride = 2 * (K / KS) + 16;
   uint8_t* hs = psm;                                                            // [16][row_stride]
   float* red = reinterpret_cast<float*>(psm + kTokChunk * row_stride);          // [8 warps][16 rows][16 tok]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int strip = blockIdx.x;
-  const int kpw = K / kPWarps;  // K per warp (<= 256): kpw / 16 k-steps
-  const int ks0 = warp * (kpw / 16);
+  const int strip = blockIdx.x / KS, ks = blockIdx.x % KS;
+  const int kpw = K / KS / kPWarps;  // K per warp (<= 256): kpw / 16 k-steps
+  const int ks0 = (ks * (K / KS)) / 16 + warp * (kpw / 16);
   // Let the next kernel of the chain start streaming its own weights now.
   pdl_launch_dependents();
   // this warp's weight fragments, loaded once (16-byte loads, streaming);
@@ -79,13 +86,41 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
   for (int i = 0; i < kMaxKPerWarp / 16; ++i)
     if (i < kpw / 16) a[i] = ldg_stream16(src + i * 32);
   pdl_wait();  // x is the previous kernel's output
+  const int kb = ks * (K / KS), kn = K / KS;  // this CTA's K range (staged columns)
   for (int c0 = 0; c0 < M; c0 += kTokChunk) {
-    // stage x rows c0..c0+15 (zero rows past M)
-    const int vecs = K / 8;
+    // stage the K range of token rows c0..c0+15 (zero rows past M)
+    const int vecs = kn / 8;
     for (int i = threadIdx.x; i < kTokChunk * vecs; i += kPThreads) {
       const int n = i / vecs, v = i % vecs;
       uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (c0 + n < M) val = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(c0 + n) * K)[v];
+      if (c0 + n < M) {
+        const int64_t off = static_cast<int64_t>(c0 + n) * K + kb + 8 * v;
+        if (x) {
+          val = *reinterpret_cast<const uint4*>(x + off);
+        } else {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = 0.f;
+          for (int q = 0; q < KSin; ++q) {
+            const float4 p0 = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off));
+            const float4 p1 = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off + 4));
+            f[0] += p0.x; f[1] += p0.y; f[2] += p0.z; f[3] += p0.w;
+            f[4] += p1.x; f[5] += p1.y; f[6] += p1.z; f[7] += p1.w;
+          }
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float u0 = f[2 * e], u1 = f[2 * e + 1];
+            if (xbias) {
+              u0 += __bfloat162float(__ushort_as_bfloat16(xbias[kb + 8 * v + 2 * e]));
+              u1 += __bfloat162float(__ushort_as_bfloat16(xbias[kb + 8 * v + 2 * e + 1]));
+            }
+            const __nv_bfloat162 h = __floats2bfloat162_rn(u0 / (1.f + expf(-u0)), u1 / (1.f + expf(-u1)));
+            w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          val = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
       *reinterpret_cast<uint4*>(hs + n * row_stride + v * 16) = val;
     }
     __syncthreads();
@@ -93,7 +128,7 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
 #pragma unroll
     for (int i = 0; i < kMaxKPerWarp / 16; ++i) {
       if (i < kpw / 16) {
-        const int k = (ks0 + i) * 16 + 2 * t;
+        const int k = warp * kpw + i * 16 + 2 * t;  // within the staged range
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const uint8_t* hrow = hs + (nt * 8 + g) * row_stride;
@@ -118,35 +153,85 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
 #pragma unroll
       for (int w = 0; w < kPWarps; ++w) v += red[(w * 16 + row) * kTokChunk + col];
       const int orow = strip * 16 + row, m = c0 + col;
-      if (m < M) {
-        if (bias) v += __bfloat162float(__ushort_as_bfloat16(bias[orow]));
-        if (mode == 0) {
-          out_bf16[static_cast<int64_t>(m) * R + orow] = __bfloat16_as_ushort(__float2bfloat16(v / (1.f + expf(-v))));
-        } else {
-          out_f32[static_cast<int64_t>(m) * R + orow] = v;
-        }
-      }
+      if (m < M) part[(static_cast<int64_t>(ks) * M + m) * R + orow] = v;
     }
     __syncthreads();
   }
 }
 
+// HiddenResidualExpertPredictor's middle (training/hidden_residual.py:86-103),
+// one warp per token m: a = silu(sum of the first linear's KS partial slices
+// + b1), state = LayerNorm(a) (biased variance, eps, weight, bias), then for
+// every future delta f the classifier's input column m * F + f =
+// bf16(silu(state + layer_emb[layer_ids[m]] + delta_emb[f])). Width <= 2048.
+__global__ void hr_context_kernel(const float* __restrict__ part, int KS, const uint16_t* __restrict__ b1,
+                                  int M, int W, const uint16_t* __restrict__ ln_w, const uint16_t* __restrict__ ln_b,
+                                  float eps, const uint16_t* __restrict__ layer_emb, int num_layers,
+                                  const int32_t* __restrict__ layer_ids, const uint16_t* __restrict__ delta_emb,
+                                  int F, uint16_t* __restrict__ ctx) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (m >= M) return;
+  constexpr int kPer = 2048 / 32;
+  float a[kPer];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int c = lane + 32 * j;
+    a[j] = 0.f;
+    if (c < W) {
+      float v = b1 ? __bfloat162float(__ushort_as_bfloat16(b1[c])) : 0.f;
+      for (int q = 0; q < KS; ++q) v += __ldcg(part + (static_cast<int64_t>(q) * M + m) * W + c);
+      a[j] = v / (1.f + expf(-v));
+      sum += a[j];
+    }
+  }
+  const float mean = warp_sum(sum) / W;
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (lane + 32 * j < W) var += (a[j] - mean) * (a[j] - mean);
+  const float rstd = rsqrtf(warp_sum(var) / W + eps);
+  int lid = layer_ids ? layer_ids[m] : 0;
+  lid = lid < 0 ? 0 : (lid >= num_layers ? num_layers - 1 : lid);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int c = lane + 32 * j;
+    if (c >= W) continue;
+    float st = (a[j] - mean) * rstd;
+    if (ln_w) st *= __bfloat162float(__ushort_as_bfloat16(ln_w[c]));
+    if (ln_b) st += __bfloat162float(__ushort_as_bfloat16(ln_b[c]));
+    st += __bfloat162float(__ushort_as_bfloat16(layer_emb[static_cast<int64_t>(lid) * W + c]));
+    for (int f = 0; f < F; ++f) {
+      const float u = st + __bfloat162float(__ushort_as_bfloat16(delta_emb[static_cast<int64_t>(f) * W + c]));
+      ctx[(static_cast<int64_t>(m) * F + f) * W + c] = __bfloat16_as_ushort(__float2bfloat16(u / (1.f + expf(-u))));
+    }
+  }
+}
+
 // Top-k of each row of E logits (one warp per row; E <= 1024, k <= 32):
-// descending, exact ties to the lower index.
-__global__ void topk_rows_kernel(const float* __restrict__ logits, int rows, int E, int k,
+// descending, exact ties to the lower index. The logits are finished here
+// from the second linear's KS partial slices part[ks][m][f * E + i] plus the
+// bias, and written out when `logits` is given.
+__global__ void topk_rows_kernel(const float* __restrict__ part, int KS, const uint16_t* __restrict__ bias,
+                                 int bias_f_stride, int M, int F, int E, int k, float* __restrict__ logits,
                                  int32_t* __restrict__ ids) {
   extern __shared__ float tv[];  // [warps][E]
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (row >= rows) return;
+  if (row >= M * F) return;
   float* v = tv + warp * E;
-  const float* src = logits + static_cast<int64_t>(row) * E;
+  const int m = row / F, f = row % F;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int i = lane; i < E; i += 32) {
-    const float x = src[i];
+    float x = bias ? __bfloat162float(__ushort_as_bfloat16(bias[f * bias_f_stride + i])) : 0.f;
+    for (int q = 0; q < KS; ++q) x += __ldcg(part + (static_cast<int64_t>(q) * M + m) * F * E + f * E + i);
     v[i] = x;
+    if (logits) logits[static_cast<int64_t>(row) * E + i] = x;
     if (x > bv) {
       bv = x;
       bi = i;
@@ -193,9 +278,18 @@ int predictor_pack(const uint16_t* w, int rows, int cols, uint16_t* out, cudaStr
   return launch_status();
 }
 
+// K-splits of one linear (rows R, inner K): enough CTAs to cover the 148 SMs
+// (at least ~200 CTAs), each warp keeping a multiple of 16 of K (at most 256).
+int predictor_ks(int R, int K) {
+  int ks = 1;
+  while (ks < kMaxPredictorKs && (R / 16) * ks < 200 && (K / (2 * ks)) % (16 * kPWarps) == 0) ks *= 2;
+  while (K / ks / kPWarps > kMaxKPerWarp) ks *= 2;
+  return ks;
+}
+
 int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const uint16_t* b1, int width,
                   const uint16_t* w2p, const uint16_t* b2, int F, int E, int k, float* logits, int32_t* ids,
-                  uint16_t* hidden2, cudaStream_t st) {
+                  float* part1, float* part2, cudaStream_t st) {
   static int configured_dev = -1;
   static size_t configured_smem = 0;
   int dev = 0;
@@ -219,23 +313,84 @@ int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const ui
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(width / 16);
-  cfg.dynamicSmemBytes = gemv_smem(H);
-  if (cudaLaunchKernelEx(&cfg, gemv_kernel, h, M, H, reinterpret_cast<const uint4*>(w1p), b1, width, 0, hidden2,
-                         static_cast<float*>(nullptr)) != cudaSuccess)
+  const int ks1 = predictor_ks(width, H), R2 = F * E, ks2 = predictor_ks(R2, width);
+  cfg.gridDim = dim3((width / 16) * ks1);
+  cfg.dynamicSmemBytes = gemv_smem(H / ks1);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, h, static_cast<const float*>(nullptr), 0,
+                         static_cast<const uint16_t*>(nullptr), M, H, reinterpret_cast<const uint4*>(w1p), width, ks1,
+                         part1) != cudaSuccess)
     return MTP_ERR_LAUNCH;
-  const int R2 = F * E;
-  cfg.gridDim = dim3(R2 / 16);
-  cfg.dynamicSmemBytes = gemv_smem(width);
-  if (cudaLaunchKernelEx(&cfg, gemv_kernel, static_cast<const uint16_t*>(hidden2), M, width,
-                         reinterpret_cast<const uint4*>(w2p), b2, R2, 1, static_cast<uint16_t*>(nullptr), logits) !=
-      cudaSuccess)
+  cfg.gridDim = dim3((R2 / 16) * ks2);
+  cfg.dynamicSmemBytes = gemv_smem(width / ks2);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, static_cast<const uint16_t*>(nullptr), static_cast<const float*>(part1),
+                         ks1, b1, M, width, reinterpret_cast<const uint4*>(w2p), R2, ks2, part2) != cudaSuccess)
     return MTP_ERR_LAUNCH;
   const int rows = M * F, wpb = 4;
   cfg.blockDim = dim3(wpb * 32);
   cfg.gridDim = dim3((rows + wpb - 1) / wpb);
   cfg.dynamicSmemBytes = static_cast<size_t>(wpb) * E * 4;
-  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(logits), rows, E, k, ids) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(part2), ks2, b2, E, M, F, E, k, logits,
+                         ids) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
+  return launch_status();
+}
+
+int predictor_hr_run(const uint16_t* h, const int32_t* layer_ids, int M, int H, const uint16_t* w1p,
+                     const uint16_t* b1, int width, const uint16_t* ln_w, const uint16_t* ln_b, float eps,
+                     const uint16_t* layer_emb, int num_layers, const uint16_t* delta_emb, int F,
+                     const uint16_t* wcp, const uint16_t* bc, int E, int k, float* logits, int32_t* ids, float* part1,
+                     uint16_t* ctx, float* part2, cudaStream_t st) {
+  static int configured_dev = -1;
+  static size_t configured_smem = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MTP_ERR_CUDA;
+  const size_t smem = gemv_smem(H > width ? H : width);
+  if (configured_dev != dev || configured_smem < smem) {
+    if (cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return MTP_ERR_CUDA;
+    configured_dev = dev;
+    configured_smem = smem;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kPThreads);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // encoder linear (W1 [width, H]) -> fp32 partials
+  const int ks1 = predictor_ks(width, H);
+  cfg.gridDim = dim3((width / 16) * ks1);
+  cfg.dynamicSmemBytes = gemv_smem(H / ks1);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, h, static_cast<const float*>(nullptr), 0,
+                         static_cast<const uint16_t*>(nullptr), M, H, reinterpret_cast<const uint4*>(w1p), width, ks1,
+                         part1) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
+  // SiLU, LayerNorm, layer and delta embeddings, SiLU -> bf16 columns
+  const int wpb = 4;
+  cfg.blockDim = dim3(wpb * 32);
+  cfg.gridDim = dim3((M + wpb - 1) / wpb);
+  cfg.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&cfg, hr_context_kernel, static_cast<const float*>(part1), ks1, b1, M, width, ln_w, ln_b,
+                         eps, layer_emb, num_layers, layer_ids, delta_emb, F, ctx) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
+  // classifier (Wc [E, width]) over the M x F columns
+  const int ks2 = predictor_ks(E, width);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.gridDim = dim3((E / 16) * ks2);
+  cfg.dynamicSmemBytes = gemv_smem(width / ks2);
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel, static_cast<const uint16_t*>(ctx), static_cast<const float*>(nullptr), 0,
+                         static_cast<const uint16_t*>(nullptr), M * F, width, reinterpret_cast<const uint4*>(wcp), E,
+                         ks2, part2) != cudaSuccess)
+    return MTP_ERR_LAUNCH;
+  const int rows = M * F;
+  cfg.blockDim = dim3(wpb * 32);
+  cfg.gridDim = dim3((rows + wpb - 1) / wpb);
+  cfg.dynamicSmemBytes = static_cast<size_t>(wpb) * E * 4;
+  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(part2), ks2, bc, 0, M, F, E, k, logits,
+                         ids) != cudaSuccess)
     return MTP_ERR_LAUNCH;
   return launch_status();
 }

@@ -335,30 +335,98 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     return out
 
 
-def fused_experts(hidden_states: torch.Tensor, w1: W4A16Experts, w2=None,
+def vllm_wna16_to_gptq(w13_qweight: torch.Tensor, w2_qweight: torch.Tensor, w13_scales: torch.Tensor,
+                       w2_scales: torch.Tensor) -> dict:
+    """vLLM's moe_wna16 GPTQ tensors back to the checkpoint form.
+
+    vLLM keeps, per expert, ``qweight.T.contiguous().view(uint8)`` ([N, K/2],
+    low nibble = even k) and ``scales.T`` ([N, K/g]) (moe_wna16.py
+    create_weights and moe_wna16_weight_loader, GPTQ branch); a symmetric
+    checkpoint has no zero points there (the kernel subtracts 8), so the
+    returned qzeros hold 8 in every nibble. Shapes: w13 [E, 2I, H/2] and
+    [E, 2I, H/g], w2 [E, H, I/2] and [E, H, I/g]; returns the ``from_gptq``
+    keys (qweight [E, K/8, N] int32, qzeros [E, K/g, N/8] int32, scales
+    [E, K/g, N] fp16)."""
+    out = {}
+    for name, q, sc in (("w13", w13_qweight, w13_scales), ("w2", w2_qweight, w2_scales)):
+        if q.dtype != torch.uint8 or q.dim() != 3 or sc.dim() != 3 or q.shape[:2] != sc.shape[:2]:
+            raise ValueError(f"{name}: expected uint8 [E, N, K/2] weights and [E, N, K/g] scales, got "
+                             f"{tuple(q.shape)} {q.dtype} and {tuple(sc.shape)}")
+        e, n, k_half = q.shape
+        out[f"{name}_qweight"] = q.contiguous().view(torch.int32).transpose(1, 2).contiguous()
+        out[f"{name}_scales"] = sc.transpose(1, 2).contiguous().to(torch.float16)
+        zero8 = torch.tensor(0x88888888 - (1 << 32), dtype=torch.int32)
+        out[f"{name}_qzeros"] = zero8.expand(e, sc.shape[2], n // 8).contiguous().to(q.device)
+    return out
+
+
+_VLLM_REPACKED: dict = {}
+
+
+def experts_from_vllm_wna16(w1: torch.Tensor, w2: torch.Tensor, quant_config) -> W4A16Experts:
+    """The kernel-layout experts for vLLM's (w1, w2, quant_config) triple,
+    repacked once and cached on the identity of the four tensors (the cache
+    holds them, so an id cannot be reused while the entry lives)."""
+    s1, s2 = getattr(quant_config, "w1_scale", None), getattr(quant_config, "w2_scale", None)
+    if s1 is None or s2 is None:
+        raise ValueError("quant_config must carry w1_scale and w2_scale (vLLM int4_w4a16)")
+    if getattr(quant_config, "w1_zp", None) is not None or getattr(quant_config, "w2_zp", None) is not None:
+        raise ValueError("zero points in vLLM's moe_wna16 layout are not supported (symmetric GPTQ only)")
+    key = tuple(id(t) for t in (w1, w2, s1, s2))
+    hit = _VLLM_REPACKED.get(key)
+    if hit is not None and all(a is b for a, b in zip(hit[0], (w1, w2, s1, s2))):
+        return hit[1]
+    g = vllm_wna16_to_gptq(w1, w2, s1, s2)
+    hidden = w1.shape[2] * 2
+    experts = W4A16Experts.from_gptq(g["w13_qweight"], g["w13_qzeros"], g["w13_scales"], g["w2_qweight"],
+                                     g["w2_qzeros"], g["w2_scales"], group_size=hidden // s1.shape[2])
+    _VLLM_REPACKED[key] = ((w1, w2, s1, s2), experts)
+    return experts
+
+
+def fused_experts(hidden_states: torch.Tensor, w1, w2=None,
                   topk_weights: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
-                  inplace: bool = False, activation: str = "silu",
+                  inplace: bool = False, activation="silu",
                   apply_router_weight_on_input: bool = False, global_num_experts: int = -1,
                   expert_map: torch.Tensor | None = None, quant_config=None, *,
                   shared: SharedExpert | None = None, zero_mode: str = "raw") -> torch.Tensor:
     """vLLM ``fused_experts`` shape: routed experts given by ``topk_weights`` /
-    ``topk_ids``. ``w1`` carries both projections (the kernel-layout blob holds
-    w13 and w2 together), so ``w2`` must be None or the same object."""
-    if w2 is not None and w2 is not w1:
-        raise ValueError("w2 must be None or the same W4A16Experts as w1 (one blob per expert)")
-    if activation.lower() != "silu":
+    ``topk_ids``. Weights either as vLLM passes them for int4_w4a16 (``w1``
+    [E, 2I, H/2] and ``w2`` [E, H, I/2] uint8 in the moe_wna16 GPTQ layout,
+    ``quant_config.w1_scale`` / ``w2_scale``; repacked once, see
+    :func:`experts_from_vllm_wna16`), or as one :class:`W4A16Experts` in
+    ``w1`` (``w2`` None or the same object). ``expert_map`` [global E] maps
+    global ids to local ones (-1: not on this rank, the pair is skipped)."""
+    name = str(getattr(activation, "value", getattr(activation, "name", activation))).lower()
+    if name != "silu":
         raise ValueError(f"only SiLU is supported, got {activation!r}")
     if apply_router_weight_on_input:
         raise ValueError("apply_router_weight_on_input is not supported")
-    if expert_map is not None:
-        raise ValueError("use slot_table / expert-parallel entry points for expert_map")
-    if global_num_experts not in (-1, w1.num_experts):
-        raise ValueError("global_num_experts must equal the experts' count")
-    if topk_ids is not None and topk_ids.dtype != torch.int32:
+    if isinstance(w1, W4A16Experts):
+        if w2 is not None and w2 is not w1:
+            raise ValueError("with a W4A16Experts in w1, w2 must be None or the same object")
+        experts = w1
+    elif isinstance(w1, torch.Tensor) and isinstance(w2, torch.Tensor):
+        experts = experts_from_vllm_wna16(w1, w2, quant_config)
+        zero_mode = "sym8"
+    else:
+        raise ValueError("w1 / w2 must be vLLM int4_w4a16 tensors or one W4A16Experts")
+    if topk_ids is None or topk_weights is None:
+        raise ValueError("topk_weights and topk_ids are required")
+    if topk_ids.dtype != torch.int32:
         topk_ids = topk_ids.to(torch.int32)
-    if topk_weights is not None and topk_weights.dtype != torch.float32:
+    if topk_weights.dtype != torch.float32:
         topk_weights = topk_weights.to(torch.float32)
-    out = moe_layer_w4a16(hidden_states, None, w1, int(topk_ids.shape[1]), shared=shared,
+    if expert_map is not None:
+        if global_num_experts not in (-1, expert_map.numel()):
+            raise ValueError("expert_map must have global_num_experts entries")
+        ids = topk_ids.long()
+        ok = (ids >= 0) & (ids < expert_map.numel())
+        topk_ids = torch.where(ok, expert_map.to(ids.device)[ids.clamp(0, expert_map.numel() - 1)].long(),
+                               torch.full_like(ids, -1)).to(torch.int32)
+    elif global_num_experts not in (-1, experts.num_experts):
+        raise ValueError("global_num_experts must equal the experts' count (or give expert_map)")
+    out = moe_layer_w4a16(hidden_states, None, experts, int(topk_ids.shape[1]), shared=shared,
                           topk_weights=topk_weights.contiguous(), topk_ids=topk_ids.contiguous(),
                           zero_mode=zero_mode)
     if inplace:
@@ -417,6 +485,65 @@ class MtpPredictor:
         _lib.call("mtp_predict_topk", _p(hidden), m, self.hidden, _p(self.w1p), _p(self.b1), self.width,
                   _p(self.w2p), _p(self.b2), self.future, self.experts, top_k, _p(logits_out), _p(ids),
                   _p(ws), ws.numel(), _stream(hidden))
+        return ids
+
+
+class HiddenResidualPredictor:
+    """The reference's ``HiddenResidualExpertPredictor`` forward on the GPU
+    (training/hidden_residual.py:44-103): encoder Linear -> SiLU -> LayerNorm,
+    plus a layer embedding and a per-delta embedding, SiLU, and one shared
+    classifier over experts for every future delta; then top-k per delta.
+    ``from_module`` takes the weights of a reference module (cast to bf16)."""
+
+    def __init__(self, w1, b1, ln_weight, ln_bias, layer_emb, delta_emb, wc, bc, *, ln_eps: float = 1e-5):
+        for name, t in (("w1", w1), ("layer_emb", layer_emb), ("delta_emb", delta_emb), ("wc", wc)):
+            _check_cuda(name, t, torch.bfloat16, 2)
+        for name, t in (("b1", b1), ("ln_weight", ln_weight), ("ln_bias", ln_bias), ("bc", bc)):
+            _check_cuda(name, t, torch.bfloat16, 1)
+        self.width, self.hidden = w1.shape
+        self.experts = wc.shape[0]
+        self.num_layers, self.future = layer_emb.shape[0], delta_emb.shape[0]
+        if wc.shape[1] != self.width or layer_emb.shape[1] != self.width or delta_emb.shape[1] != self.width:
+            raise ValueError("classifier and embeddings must have width columns")
+        self.w1p = torch.empty_like(w1)
+        self.wcp = torch.empty_like(wc)
+        _lib.call("mtp_predictor_pack", _p(w1), self.width, self.hidden, _p(self.w1p), _stream(w1))
+        _lib.call("mtp_predictor_pack", _p(wc), self.experts, self.width, _p(self.wcp), _stream(wc))
+        self.b1, self.ln_weight, self.ln_bias, self.bc = b1, ln_weight, ln_bias, bc
+        self.layer_emb, self.delta_emb = layer_emb.contiguous(), delta_emb.contiguous()
+        self.ln_eps = float(ln_eps)
+
+    @classmethod
+    def from_module(cls, module, device) -> "HiddenResidualPredictor":
+        enc, ln = module.encoder[0], module.encoder[2]
+        bf = lambda t: None if t is None else t.detach().to(device=device, dtype=torch.bfloat16).contiguous()
+        return cls(bf(enc.weight), bf(enc.bias), bf(ln.weight), bf(ln.bias), bf(module.layer_embedding.weight),
+                   bf(module.delta_embedding.weight), bf(module.classifier.weight), bf(module.classifier.bias),
+                   ln_eps=float(ln.eps))
+
+    def workspace(self, m: int, device) -> torch.Tensor:
+        out = _lib.i64()
+        _lib.call("mtp_predictor_hr_workspace_size", m, self.width, self.future, self.experts, C.byref(out))
+        return torch.empty(out.value, dtype=torch.uint8, device=device)
+
+    def predict_topk(self, hidden: torch.Tensor, layer_ids: torch.Tensor | None, top_k: int, *,
+                     logits_out: torch.Tensor | None = None, ids_out: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """ids [M, future, top_k] int32; ``layer_ids`` [M] int32 (None = layer 0)."""
+        _check_cuda("hidden", hidden, torch.bfloat16, 2)
+        _check_cuda("layer_ids", layer_ids, torch.int32, 1)
+        m = hidden.shape[0]
+        if hidden.shape[1] != self.hidden:
+            raise ValueError(f"hidden must be [M, {self.hidden}]")
+        ids = ids_out if ids_out is not None else torch.empty(m, self.future, top_k, dtype=torch.int32,
+                                                              device=hidden.device)
+        _check_cuda("ids_out", ids, torch.int32)
+        _check_cuda("logits_out", logits_out, torch.float32)
+        ws = workspace if workspace is not None else self.workspace(m, hidden.device)
+        _lib.call("mtp_predict_topk_hidden_residual", _p(hidden), _p(layer_ids), m, self.hidden, _p(self.w1p),
+                  _p(self.b1), self.width, _p(self.ln_weight), _p(self.ln_bias), C.c_float(self.ln_eps),
+                  _p(self.layer_emb), self.num_layers, _p(self.delta_emb), self.future, _p(self.wcp), _p(self.bc),
+                  self.experts, top_k, _p(logits_out), _p(ids), _p(ws), ws.numel(), _stream(hidden))
         return ids
 
 

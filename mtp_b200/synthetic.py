@@ -116,3 +116,40 @@ def make_predictor(cfg: PredictorConfig, seed: int = 0, device="cpu", bias: bool
 def make_predictor_inputs(cfg: PredictorConfig, m: int, seed: int = 0, device="cpu") -> torch.Tensor:
     g = torch.Generator(device="cpu").manual_seed(10_000 + seed)
     return torch.randn(m, cfg.hidden, generator=g).to(torch.bfloat16).to(device)
+
+
+def make_gptq_snapshot(path, *, layers: int = 2, experts: int = 4, hidden: int = 256, inter: int = 128,
+                       group_size: int = 128, shards: int = 2, seed: int = 0) -> dict:
+    """A small Hugging Face style GPTQ checkpoint snapshot on disk (sharded
+    safetensors + model.safetensors.index.json) with the Qwen3 MoE expert key
+    names (model.language_model.layers.{l}.mlp.experts.{e}.{gate,up,down}_proj.
+    {qweight,qzeros,scales,g_idx}), seeded: GPTQ int4 weights and zeros of 8,
+    fp16 scales |N(0,1)| * 0.02 + 1e-3, g_idx = k // group_size. Experts are
+    spread over `shards` files. Returns the tensors by key."""
+    import json
+    from pathlib import Path
+
+    from safetensors.torch import save_file
+
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    g = torch.Generator().manual_seed(seed)
+    tensors = {}
+    for l in range(layers):
+        for e in range(experts):
+            for proj, (k, n) in (("gate_proj", (hidden, inter)), ("up_proj", (hidden, inter)),
+                                 ("down_proj", (inter, hidden))):
+                key = f"model.language_model.layers.{l}.mlp.experts.{e}.{proj}"
+                tensors[f"{key}.qweight"] = _qweight(g, (k // 8, n), "cpu")
+                tensors[f"{key}.qzeros"] = _zeros(None, (k // group_size, n // 8), "cpu", False)
+                tensors[f"{key}.scales"] = _scales(g, (k // group_size, n), "cpu")
+                tensors[f"{key}.g_idx"] = torch.arange(k, dtype=torch.int32) // group_size
+    names = sorted(tensors)
+    weight_map = {}
+    for s in range(shards):
+        part = {n: tensors[n] for i, n in enumerate(names) if i % shards == s}
+        fname = f"model-{s + 1:05d}-of-{shards:05d}.safetensors"
+        save_file(part, str(path / fname))
+        weight_map.update({n: fname for n in part})
+    (path / "model.safetensors.index.json").write_text(json.dumps({"metadata": {}, "weight_map": weight_map}))
+    return tensors

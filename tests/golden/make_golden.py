@@ -28,6 +28,23 @@ Fixtures:
   cache.pt          reference ``ControlledExpertCacheManager`` and
                     ``ReadyTimeExpertCacheManager`` (runtime/cache_manager.py:208-578)
                     counters after seeded issue/demand sequences.
+  predictor_hr.pt   reference ``HiddenResidualExpertPredictor`` (training/
+                    hidden_residual.py:44-103; hidden 256, 64 experts, 6 layers,
+                    future window 4, width 128, seed 7, every parameter rounded to
+                    bf16 so the kernel's bf16 copies are exact) on bf16 hidden
+                    states [9, 256] with layer ids: its state dict, inputs, fp32
+                    logits [9, 4, 64] and torch.topk(logits, 8) ids (the ranking of
+                    recall_at_m, training/predictor.py:105).
+  premap.pt         reference ``build_priority_masks`` / ``build_premap_descriptors``
+                    (runtime/premap.py:78-192) on seeded transition and MTP scores
+                    [5 tokens, 2 deltas, 3 layers, 64 experts] of 2 samples, max and
+                    mean reductions.
+  repack_manifest.json  the reference ``repack_qwen3_moe_gptq``
+                    (repack/qwen3_moe_gptq.py:201-265) on the seeded synthetic snapshot
+                    of mtp_b200.synthetic.make_gptq_snapshot (2 layers, 4 experts,
+                    H=256, I=128, g=128, 2 shards, seed 0): its manifest.jsonl records
+                    (per-tensor shape, dtype, sha256, source fields) and summary.json
+                    without the machine paths.
 """
 from __future__ import annotations
 
@@ -211,17 +228,79 @@ def gen_cache():
     torch.save(cases, HERE / "cache.pt")
 
 
+def gen_predictor_hr():
+    from mtp_expert_prefetch.training.hidden_residual import HiddenResidualExpertPredictor
+    torch.manual_seed(7)
+    mod = HiddenResidualExpertPredictor(hidden_size=256, num_experts=64, num_layers=6, future_window=4, width=128)
+    mod.eval()
+    with torch.no_grad():
+        for prm in mod.parameters():
+            prm.copy_(prm.to(torch.bfloat16).to(torch.float32))
+        # a LayerNorm affine that is not the identity
+        mod.encoder[2].weight.copy_((1.0 + 0.1 * torch.randn(128)).to(torch.bfloat16).to(torch.float32))
+        mod.encoder[2].bias.copy_((0.1 * torch.randn(128)).to(torch.bfloat16).to(torch.float32))
+        hidden = torch.randn(9, 256).to(torch.bfloat16)
+        layer_ids = torch.tensor([0, 5, 2, 3, 3, 1, 4, 0, 5], dtype=torch.int32)
+        logits = mod(hidden.to(torch.float32), layer_ids=layer_ids.long())
+    ids = torch.topk(logits, 8, dim=-1).indices.to(torch.int32)
+    torch.save(dict(state={k: v.clone() for k, v in mod.state_dict().items()}, hidden=hidden, layer_ids=layer_ids,
+                    logits=logits, topk_ids=ids, config=dict(hidden_size=256, num_experts=64, num_layers=6,
+                                                                 future_window=4, width=128, ln_eps=1e-5)),
+               HERE / "predictor_hr.pt")
+
+
+def gen_repack():
+    import json
+    import tempfile
+
+    from mtp_expert_prefetch.repack.qwen3_moe_gptq import repack_qwen3_moe_gptq
+    sys.path.insert(0, str(ROOT))
+    from mtp_b200.synthetic import make_gptq_snapshot
+    with tempfile.TemporaryDirectory() as tmp:
+        snap, out = Path(tmp) / "snapshot", Path(tmp) / "repacked"
+        make_gptq_snapshot(snap, layers=2, experts=4, hidden=256, inter=128, group_size=128, shards=2, seed=0)
+        repack_qwen3_moe_gptq(snap, out, num_experts=4)
+        records = [json.loads(line) for line in (out / "manifest.jsonl").read_text().splitlines() if line.strip()]
+        summary = json.loads((out / "summary.json").read_text())
+    for key in ("snapshot_path", "output_dir"):
+        summary.pop(key, None)
+    (HERE / "repack_manifest.json").write_text(json.dumps({"records": records, "summary": summary,
+                                                           "snapshot": dict(layers=2, experts=4, hidden=256,
+                                                                            inter=128, group_size=128, shards=2,
+                                                                            seed=0)}, indent=1, sort_keys=True))
+
+
+def gen_premap():
+    from mtp_expert_prefetch.runtime.premap import build_premap_descriptors, build_priority_masks
+    g = torch.Generator().manual_seed(13)
+    trans = torch.rand(5, 2, 3, 64, generator=g)
+    mtp = torch.randn(5, 2, 3, 64, generator=g)
+    samples = torch.tensor([0, 0, 1, 1, 1])
+    masks = build_priority_masks(trans, mtp)
+    out = dict(transition=trans, mtp=mtp, samples=samples, masks={k: v.clone() for k, v in masks.items()})
+    for red in ("max", "mean"):
+        d = build_premap_descriptors(trans, mtp, samples, reduce=red)
+        out[f"descriptors_{red}"] = [(x.sample_idx, x.layer_idx, x.expert_id, x.priority, x.source, x.score)
+                                     for x in d]
+    torch.save(out, HERE / "premap.pt")
+
+
+GENERATORS = {"gptq_dequant": lambda: gen_dequant(None), "moe_small": lambda: gen_moe_small(),
+              "config0": lambda: gen_config0(), "router": lambda: gen_router(), "cache": lambda: gen_cache(),
+              "predictor_hr": lambda: gen_predictor_hr(), "repack": lambda: gen_repack(),
+              "premap": lambda: gen_premap()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
+    ap.add_argument("--only", nargs="*", choices=sorted(GENERATORS), help="generate only these fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
     torch.manual_seed(0)
-    gen_dequant(None)
-    gen_moe_small()
-    gen_config0()
-    gen_router()
-    gen_cache()
+    for name, gen in GENERATORS.items():
+        if not args.only or name in args.only:
+            gen()
     for f in sorted(HERE.glob("*.pt")):
         print(f.name, f.stat().st_size)
 

@@ -255,3 +255,94 @@ def test_expert_counts_and_top_k_match_oracle(cuda_device, e, k, m):
     ref = o.moe_tokens(x.float(), torch.as_tensor(oids), torch.as_tensor(ow))
     check(out, ref)
 
+
+
+def test_fused_experts_takes_vllm_wna16_tensors_and_expert_map(cuda_device):
+    """vLLM's call form for int4_w4a16: fused_experts(hidden, w1, w2, topk
+    weights / ids, quant_config=...) with w1 [E, 2I, H/2] and w2 [E, H, I/2]
+    uint8 in the moe_wna16 GPTQ layout (tracing/vllm_router_trace.py:19330-19840
+    replaces exactly this call) gives the same bits as the layer on the
+    checkpoint tensors; with an expert_map, pairs of experts mapped to -1 are
+    skipped (vLLM's expert-parallel convention)."""
+    from types import SimpleNamespace
+
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    from test_vllm_layout import vllm_layout
+    cfg = LayerConfig(num_experts=16, hidden=512, inter=256, top_k=4, tokens=(24,))
+    experts, _ = make_layer(cfg, seed=61, device=cuda_device)
+    w1, w2, s1, s2 = vllm_layout(experts)
+    qc = SimpleNamespace(w1_scale=s1, w2_scale=s2, w1_zp=None, w2_zp=None, block_shape=[0, 128])
+    x, logits = make_inputs(cfg, 24, seed=62, device=cuda_device)
+    tw, ti, _ = mtp_b200.topk_softmax(logits, 4, True)
+    a = mtp_b200.fused_experts(x, w1, w2, tw, ti, quant_config=qc)
+    # the checkpoint tensors with their scales rounded as vLLM holds them (bf16)
+    g = mtp_b200.vllm_wna16_to_gptq(w1, w2, s1, s2)
+    ref_experts = mtp_b200.W4A16Experts.from_gptq(*(g[k] for k in KEYS))
+    b = mtp_b200.moe_layer_w4a16(x, None, ref_experts, 4, topk_weights=tw, topk_ids=ti, zero_mode="sym8")
+    assert torch.equal(a, b)
+    assert mtp_b200.experts_from_vllm_wna16(w1, w2, qc) is mtp_b200.experts_from_vllm_wna16(w1, w2, qc)
+    # expert_map: global 16 experts, this "rank" owns the even ones as local 0..7
+    emap = torch.full((16,), -1, dtype=torch.int32, device=cuda_device)
+    emap[0::2] = torch.arange(8, dtype=torch.int32, device=cuda_device)
+    local = {k: v[0::2].contiguous() for k, v in experts.items()}
+    lw1, lw2, ls1, ls2 = vllm_layout(local)
+    lqc = SimpleNamespace(w1_scale=ls1, w2_scale=ls2, w1_zp=None, w2_zp=None, block_shape=[0, 128])
+    c = mtp_b200.fused_experts(x, lw1, lw2, tw, ti, global_num_experts=16, expert_map=emap, quant_config=lqc)
+    mapped = torch.where(ti % 2 == 0, ti // 2, torch.full_like(ti, -1))
+    lg = mtp_b200.vllm_wna16_to_gptq(lw1, lw2, ls1, ls2)
+    d = mtp_b200.moe_layer_w4a16(x, None, mtp_b200.W4A16Experts.from_gptq(*(lg[k] for k in KEYS)), 4,
+                                 topk_weights=tw, topk_ids=mapped, zero_mode="sym8")
+    assert torch.equal(c, d)
+
+
+def test_repacked_store_layer_runs_the_kernel(cuda_device, tmp_path):
+    """A layer loaded from a repacked checkpoint store (sha256-verified) gives
+    the same kernel blobs as the GPTQ tensors repacked directly, and the layer
+    output matches the oracle on those tensors."""
+    import mtp_b200
+    from mtp_b200 import checkpoint as ck
+    from mtp_b200.synthetic import LayerConfig, make_gptq_snapshot, make_inputs
+    make_gptq_snapshot(tmp_path / "snap", layers=1, experts=8, hidden=512, inter=256, shards=2, seed=4)
+    ck.repack_snapshot(tmp_path / "snap", tmp_path / "out", num_experts=8)
+    store = ck.RepackedStore(tmp_path / "out")
+    w = store.load_layer(0, cuda_device)
+    g, group = store.gptq_layer(0)
+    direct = mtp_b200.W4A16Experts.from_gptq(*(g[k].to(cuda_device) for k in KEYS), group_size=group)
+    assert torch.equal(w.blobs, direct.blobs)
+    cfg = LayerConfig(num_experts=8, hidden=512, inter=256, top_k=2, tokens=(6,))
+    x, logits = make_inputs(cfg, 6, seed=8)
+    out = mtp_b200.moe_layer_w4a16(x.to(cuda_device), logits.to(cuda_device), w, 2)
+    ow, oids, _ = orouter.topk_softmax(logits.numpy(), 2, True)
+    ref = olayer.MoeLayerOracle(g, None).moe_tokens(x.float(), torch.as_tensor(oids), torch.as_tensor(ow))
+    check(out, ref)
+
+
+def test_vllm_shim_routes_vllm_fused_experts(cuda_device):
+    """With mtp_b200.vllm_shim installed, vLLM's own public fused_experts
+    (int4_w4a16 quant config, its custom-op dispatch) computes through this
+    library: same bits as mtp_b200.fused_experts, and the call is counted as
+    routed. Uninstalled, vLLM's function is back."""
+    fm = pytest.importorskip("vllm.model_executor.layers.fused_moe.fused_moe")
+    cfg_mod = pytest.importorskip("vllm.model_executor.layers.fused_moe.config")
+    import mtp_b200
+    from mtp_b200 import vllm_shim
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    from test_vllm_layout import vllm_layout
+    cfg = LayerConfig(num_experts=16, hidden=512, inter=256, top_k=4, tokens=(12,))
+    experts, _ = make_layer(cfg, seed=71, device=cuda_device)
+    w1, w2, s1, s2 = vllm_layout(experts)
+    qc = cfg_mod.int4_w4a16_moe_quant_config(s1, s2, None, None, [0, 128])
+    x, logits = make_inputs(cfg, 12, seed=72, device=cuda_device)
+    tw, ti, _ = mtp_b200.topk_softmax(logits, 4, True)
+    want = mtp_b200.fused_experts(x, w1, w2, tw, ti, quant_config=qc)
+    vllm_shim.install()
+    try:
+        before = vllm_shim.stats.routed_calls
+        got = fm.fused_experts(x, w1, w2, tw, ti, quant_config=qc)
+        torch.cuda.synchronize()
+        assert vllm_shim.stats.routed_calls == before + 1
+        assert torch.equal(got, want)
+    finally:
+        vllm_shim.uninstall()
+    assert not vllm_shim.installed()

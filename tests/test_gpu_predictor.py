@@ -70,3 +70,45 @@ def test_predictor_rejects_bad_shapes(cuda_device):
     assert lib.mtp_predict_topk(p, 1, 256, p, None, 256, p, None, 4, 256, 33, None, p, p, buf.numel(), None) == 2
     # workspace too small
     assert lib.mtp_predict_topk(p, 64, 256, p, None, 256, p, None, 4, 256, 8, None, p, p, 16, None) == 4
+
+
+def test_hidden_residual_predictor_matches_reference_golden(cuda_device):
+    """The reference predictor architecture (HiddenResidualExpertPredictor:
+    encoder Linear -> SiLU -> LayerNorm, layer and delta embeddings, shared
+    classifier) run by the kernel on the reference module's own weights and
+    inputs (tests/golden/predictor_hr.pt): logits within LOGIT_TOL of the
+    reference's fp32 logits and of the bf16-context oracle, top-8 ids equal to
+    the reference's on at least EXACT_ROW_FRACTION of the (token, delta)
+    rows, every other pick within tolerance of the k-th best."""
+    import mtp_b200
+    from conftest import golden
+    g = golden("predictor_hr.pt")
+    st, c = g["state"], g["config"]
+    bf = lambda t: t.to(torch.bfloat16).to(cuda_device).contiguous()
+    pred = mtp_b200.HiddenResidualPredictor(bf(st["encoder.0.weight"]), bf(st["encoder.0.bias"]),
+                                            bf(st["encoder.2.weight"]), bf(st["encoder.2.bias"]),
+                                            bf(st["layer_embedding.weight"]), bf(st["delta_embedding.weight"]),
+                                            bf(st["classifier.weight"]), bf(st["classifier.bias"]), ln_eps=c["ln_eps"])
+    m, f, e = g["logits"].shape
+    logits = torch.empty(m, f, e, dtype=torch.float32, device=cuda_device)
+    ids = pred.predict_topk(g["hidden"].to(cuda_device), g["layer_ids"].to(cuda_device), 8, logits_out=logits)
+    torch.cuda.synchronize()
+    got = logits.cpu()
+    ref = g["logits"]
+    scale = ref.abs().max().item()
+    orc = opred.hidden_residual_logits(g["hidden"], g["layer_ids"], st["encoder.0.weight"], st["encoder.0.bias"],
+                                       st["encoder.2.weight"], st["encoder.2.bias"], c["ln_eps"],
+                                       st["layer_embedding.weight"], st["delta_embedding.weight"],
+                                       st["classifier.weight"], st["classifier.bias"])
+    assert (got - orc).abs().max().item() <= LOGIT_TOL * scale
+    assert (got - ref).abs().max().item() <= LOGIT_TOL * scale
+    gi, ri = ids.cpu().numpy(), g["topk_ids"].numpy()
+    exact = 0
+    for i in range(m):
+        for j in range(f):
+            if np.array_equal(gi[i, j], ri[i, j]):
+                exact += 1
+                continue
+            kth = np.sort(ref[i, j].numpy())[::-1][7]
+            assert (ref[i, j].numpy()[gi[i, j]] >= kth - LOGIT_TOL * scale).all()
+    assert exact >= EXACT_ROW_FRACTION * m * f

@@ -31,3 +31,21 @@ def test_oracle_ties_go_to_lower_id():
     row = np.zeros((1, 16), dtype=np.float32)
     row[0, [3, 7, 9]] = 1.0
     assert topk_order(row, 2).tolist() == [[3, 7]]
+
+
+def test_hidden_residual_oracle_matches_reference_golden():
+    """oracle.predictor.hidden_residual_logits (fp32, no bf16 rounding) equals
+    the reference HiddenResidualExpertPredictor's own logits (fixture made by
+    tests/golden/make_golden.py) and ranks the same top-8."""
+    import torch
+
+    from conftest import golden
+    from oracle import predictor as opred
+    g = golden("predictor_hr.pt")
+    st, c = g["state"], g["config"]
+    lg = opred.hidden_residual_logits(g["hidden"], g["layer_ids"], st["encoder.0.weight"], st["encoder.0.bias"],
+                                      st["encoder.2.weight"], st["encoder.2.bias"], c["ln_eps"],
+                                      st["layer_embedding.weight"], st["delta_embedding.weight"],
+                                      st["classifier.weight"], st["classifier.bias"], round_context_bf16=False)
+    torch.testing.assert_close(lg, g["logits"], rtol=1e-5, atol=1e-5)
+    assert torch.equal(torch.topk(lg, 8, dim=-1).indices.to(torch.int32), g["topk_ids"])
