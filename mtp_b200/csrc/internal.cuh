@@ -15,7 +15,7 @@ constexpr int kWsInts = 4 + 8 * kWsBlocks;
 //   [3] flags (bit 0 shared expert, bit 1 blob in host memory),
 //   [4..] pair ids (row of h / y), -1 for padding.
 
-// One quantised x row: H high bytes, H offset low bytes, the per-group sums
+// One quantised x row: H high-digit bytes, H low-digit bytes, the per-group sums
 // of the 16-bit values (int32, room for groups of 64), the row scale (fp32)
 // and padding to 16 bytes. The meta travels with the row in one bulk copy.
 __host__ __device__ constexpr uint32_t xq_row_bytes(int H) {

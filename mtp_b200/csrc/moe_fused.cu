@@ -23,24 +23,28 @@
 //              unit of a segment it waits until every W1 unit of that segment
 //              has published its h columns;
 //     warps 0-7  dequant - quantise each new block of operand rows in place to
-//              16-bit integers laid out as the MMA's B operand (a signed high
-//              byte plane and an unsigned low byte plane, K-major 8x16-byte
-//              core matrices, one scale per row, sums per quantisation group),
+//              16-bit integers laid out as the MMA's B operand (v = 256 hi +
+//              lo with both digits signed bytes: a high and a low digit
+//              plane, K-major 8x16-byte core matrices, one scale per row,
+//              sums of v per quantisation group),
 //              and unpack each stage's int4 weights to u8 straight into tensor
 //              memory (the MMA's A operand, lane = weight row);
-//     warp 12  MMA issuer - one thread issues tcgen05.mma kind::i8 (M=128,
-//              N=8, K=32; A u8 from tensor memory, B from shared memory) for
-//              the high and the low byte plane into per-group int32
-//              accumulators in tensor memory, and commits each stage to an
-//              mbarrier;
+//     warps 12, 15  MMA issuers (alternate stages) - one thread each issues
+//              tcgen05.mma kind::i8 (M=128, N=16 = the 8 rows of the high
+//              digit plane then the 8 of the low one, K=32; A u8 from tensor
+//              memory, B s8 from shared memory) into per-group int32
+//              accumulators in tensor memory, and commits each stage to
+//              mbarriers;
 //     warps 8-11 epilogue - read the accumulators back (tcgen05.ld), fold
 //              zero point, group scale and row scale in fp32 per group:
 //              acc += s_g * (256 * D_hi + D_lo - z_g * sum_g(x)), then at the
 //              end of a unit write h = silu(gate) * up (W1) or y = acc * w
 //              (W2).
-//   Tensor memory holds a ring of 4 slots, each the u8 A tile of one stage
-//   and the group accumulators of that stage, so dequant, MMA and epilogue of
-//   consecutive stages overlap.
+//   Tensor memory holds two rings: A slots (the u8 tile of one stage; freed by
+//   the MMA's commit) and accumulator slots (the group accumulators of one
+//   stage; freed by the epilogue), so dequant, MMA and epilogue of
+//   consecutive stages overlap and the dequant warps never wait for the
+//   epilogue.
 //
 // Work units, in this order (each CTA takes a contiguous range of each list;
 // a work segment is one token block, so ranges balance and consecutive units
@@ -83,11 +87,10 @@ constexpr int kRouteWarps = 7;      // warps 0-6 route, 7-13 gate
 constexpr int kMaxStages = 8;
 constexpr int kMaxASlots = 4;
 constexpr int kMaxDSlots = 8;
-constexpr int kQCols = 4;
 constexpr int kTmemCols = 512;
 __host__ __device__ constexpr int accs_for(int sk) { return sk >= 512 ? 4 : 2; }
 __host__ __device__ constexpr int aslots_for(int sk) { return sk >= 512 ? 2 : 4; }
-__host__ __device__ constexpr int dslot_cols(int sk) { return accs_for(sk) * 16 + 2 * kQCols; }
+__host__ __device__ constexpr int dslot_cols(int sk) { return accs_for(sk) * 16; }
 __host__ __device__ constexpr int dslots_for(int sk) {
   return (kTmemCols - aslots_for(sk) * (sk / 4)) / dslot_cols(sk) < kMaxDSlots
              ? (kTmemCols - aslots_for(sk) * (sk / 4)) / dslot_cols(sk)
@@ -99,7 +102,6 @@ struct StageCfg {
   static constexpr int aslots = aslots_for(SK);
   static constexpr int dslots = dslots_for(SK);
   static constexpr uint32_t acols = SK / 4;
-  static constexpr uint32_t dcols = accs * 16;
   static constexpr uint32_t dbase = aslots * acols;
   static constexpr uint32_t dstride = dslot_cols(SK);
 };
@@ -299,7 +301,9 @@ __device__ __forceinline__ int cta_exclusive_scan(int v, int* total, int* tmp) {
 // Router for one token by one warp with the logits in registers (E <= 256:
 // eight per lane, lane l holding ids l, l + 32, ...). Same selection as
 // router_warp below: softmax over all E, top-k descending, exact ties to the
-// lower expert; the probability is exp(v - max) times 1 / sum.
+// lower expert; the probability is exp(v - max) / sum, the same operations in
+// the same order as the standalone router (route.cuh router_token), so both
+// give the same bits.
 __device__ __forceinline__ void router_warp_regs(const float* __restrict__ row, int E, int k, int renorm,
                                                  float* w_out, int* id_out) {
   const int lane = threadIdx.x & 31;
@@ -318,7 +322,6 @@ __device__ __forceinline__ void router_warp_regs(const float* __restrict__ row, 
   for (int j = 0; j < 8; ++j)
     if (32 * j + lane < E) s += expf(x[j] - mx);
   s = warp_sum(s);
-  const float inv_s = 1.f / s;
   // each lane's best untaken candidate; `taken` marks the lane's picked slots
   uint32_t taken = 0;
   float bv = -INFINITY;
@@ -343,7 +346,7 @@ __device__ __forceinline__ void router_warp_regs(const float* __restrict__ row, 
         wi = oi;
       }
     }
-    const float p = expf(wv - mx) * inv_s;
+    const float p = expf(wv - mx) / s;
     wsum += p;
     if (lane == r) {
       my_w = p;
@@ -433,17 +436,24 @@ __device__ __forceinline__ void router_warp(const float* __restrict__ row, int E
   *id_out = my_id;
 }
 
-// 16-bit integers v -> the high bytes and the offset low bytes (v & 255) ^ 128
-// (= lo - 128 as a signed byte) of four values, packed little-endian.
+// Largest |v| of the 16-bit activation integers: v = 256 * hi + lo with both
+// digits signed bytes (lo in [-128, 127], hi = (v + 128) >> 8) needs
+// v <= 127 * 256 + 127.
+constexpr float kVMax = 32639.f;
+
+// 16-bit integers v (|v| <= kVMax) -> the signed-digit bytes hi = (v + 128) >> 8
+// and lo = v - 256 * hi (the low byte of v read as signed) of four values,
+// packed little-endian. sum_k q v = 256 sum_k q hi + sum_k q lo with both MMAs
+// signed, so no correction term is needed.
 __device__ __forceinline__ void pack_hilo(int v0, int v1, int v2, int v3, uint32_t& hw, uint32_t& lw) {
-  hw = __byte_perm(__byte_perm(v0, v1, 0x0051), __byte_perm(v2, v3, 0x0051), 0x5410);
-  lw = __byte_perm(__byte_perm(v0, v1, 0x0040), __byte_perm(v2, v3, 0x0040), 0x5410) ^ 0x80808080u;
+  hw = __byte_perm(__byte_perm(v0 + 128, v1 + 128, 0x0051), __byte_perm(v2 + 128, v3 + 128, 0x0051), 0x5410);
+  lw = __byte_perm(__byte_perm(v0, v1, 0x0040), __byte_perm(v2, v3, 0x0040), 0x5410);
 }
 
 // Quantise one token's x row (one warp, lane holding the 8-element vectors
-// lane + 32 j) to 16-bit integers v = round(x / sx), sx = max|x| / 32767, and
-// store them as a high-byte row then an offset low-byte row, followed by the
-// per-group sums of v and sx (one xq_row_bytes(H) row per token).
+// lane + 32 j) to 16-bit integers v = round(x / sx), sx = max|x| / kVMax, and
+// store them as a high-digit row then a low-digit row (pack_hilo), followed by
+// the per-group sums of v and sx (one xq_row_bytes(H) row per token).
 __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const uint4 (&xv)[8]) {
   const int lane = threadIdx.x & 31;
   const int nvec = a.H / 8;
@@ -457,7 +467,7 @@ __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const 
     }
   }
   mx = warp_max(mx);
-  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  const float inv = mx > 0.f ? kVMax / mx : 0.f;
   uint8_t* row = a.xq + static_cast<int64_t>(t) * xq_row_bytes(a.H);
   int32_t* gsum = reinterpret_cast<int32_t*>(row + 2 * a.H);
   const int lpg = a.G / 8;  // lanes (8-element vectors) per group: 8 or 16
@@ -485,7 +495,7 @@ __device__ __forceinline__ void quantize_token(const FusedArgs& a, int t, const 
     for (int o = 1; o < lpg; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
     if ((lane & (lpg - 1)) == 0 && lane + 32 * j < nvec) gsum[(lane + 32 * j) / lpg] = sum;
   }
-  if (lane == 0) *reinterpret_cast<float*>(row + 2 * a.H + a.H / 16) = mx / 32767.f;
+  if (lane == 0) *reinterpret_cast<float*>(row + 2 * a.H + a.H / 16) = mx / kVMax;
 }
 
 // Phase 1: route this CTA's tokens, count and list the (token, slot) pairs per
@@ -878,7 +888,7 @@ __device__ void operand_producer(const FusedArgs& a, Ctrl& cb, const int* table,
 // dequant warps (0-7): operand quantisation and the A tiles in tensor memory
 // ---------------------------------------------------------------------------
 // W1 operand: the 8 token rows arrive already quantised (xq rows: K high
-// bytes, K offset low bytes, group sums, scale; see quantize_token); take the
+// digits, K low digits, group sums, scale; see quantize_token); take the
 // meta out, then rearrange them in place
 // into the MMA's B layout, both planes K-major in 8-row x 16-byte core
 // matrices ((n, k) at (k / 16) * 128 + n * 16 + k % 16, high plane at [0, 8K),
@@ -922,8 +932,8 @@ __device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* p
 
 // W2 operand: the 8 pair rows arrive as fp32 W1 sums (K gate values, K up
 // values, the combine weight, padding); form h = bf16(silu(gate) * up) and
-// quantise it in place to 16-bit integers v = 256 * hi + lo' + 128, laid out
-// as the B planes above, with one scale per row (times the combine weight)
+// quantise it in place to 16-bit integers v = 256 * hi + lo (pack_hilo), laid
+// out as the B planes above, with one scale per row (times the combine weight)
 // and per-group sums of v. Thread (warp w, lane = 4n + q) owns
 // the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i.
 template <int G>
@@ -960,7 +970,7 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < kDQ; ++j) amax = fmaxf(amax, meta.amax[j][n]);
-  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+  const float inv = amax > 0.f ? kVMax / amax : 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i < iters) {  // warp-uniform
@@ -983,7 +993,7 @@ __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta
   if (t < kFBM) {
     float m = 0.f;
     for (int j = 0; j < kDQ; ++j) m = fmaxf(m, meta.amax[j][t]);
-    meta.sx[t] = m / 32767.f * cw;
+    meta.sx[t] = m / kVMax * cw;
   }
   fence_proxy_async_shared();  // the plane stores are read by the tensor cores
   named_bar_sync(kBarDequant, kDQ * 32);
@@ -996,12 +1006,11 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
   const int quad = warp & 3, half = warp >> 2;
   const int r = 32 * quad + lane;  // weight row = tensor-memory lane
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
-  constexpr int chunks = SK / 32, my_chunks = chunks / 2, gps = SK / G;
+  constexpr int chunks = SK / 32, my_chunks = chunks / 2;
   using C = StageCfg<SK>;
-  static_assert(gps <= kQCols, "a stage's groups fit the sum columns");
   const uint32_t tmem = cb.tmem;
-  int st = 0, ta = 0, td = 0, xb = 0;
-  uint32_t ph = 0, aph = 0, dph = 0, xph = 0;
+  int st = 0, ta = 0, xb = 0;
+  uint32_t ph = 0, aph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int K = pass == 0 ? a.H : a.I;
@@ -1023,9 +1032,6 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
         tc_fence_after();
         const uint32_t sbase = smem_u32(stages + static_cast<size_t>(st) * a.stage_bytes);
         const uint32_t tcol = tmem + lane_addr + ta * C::acols;
-        uint32_t qsum[gps];
-#pragma unroll
-        for (int g = 0; g < gps; ++g) qsum[g] = 0;
         // the stage's words of this thread's row and K half, loaded at once so
         // the shared-memory stage can go back to the producer before the
         // unpack (a stage of an expert without weights holds stale words; the
@@ -1039,32 +1045,16 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
         for (int cp = 0; cp < my_chunks; cp += 2) {
           const int c0 = half * my_chunks + cp;
           uint32_t v[16];
-          int qs = 0;  // sum of the 64 int4 values of the two chunks
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const uint32_t w4[4] = {wq[cp + cc].x, wq[cp + cc].y, wq[cp + cc].z, wq[cp + cc].w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t lo = w4[j] & 0x0F0F0F0Fu, hi = (w4[j] >> 4) & 0x0F0F0F0Fu;
-              v[cc * 8 + 2 * j] = lo;
-              v[cc * 8 + 2 * j + 1] = hi;
-              qs = __dp4a(static_cast<int>(lo + hi), 0x01010101, qs);  // byte sums <= 30: no carry between bytes
+              v[cc * 8 + 2 * j] = w4[j] & 0x0F0F0F0Fu;
+              v[cc * 8 + 2 * j + 1] = (w4[j] >> 4) & 0x0F0F0F0Fu;
             }
           }
           tmem_st16(tcol + c0 * 8, v);
-#pragma unroll
-          for (int g = 0; g < gps; ++g) qsum[g] += ((c0 * 32) / G == g) ? static_cast<uint32_t>(qs) : 0u;
-        }
-        // this K half's share of each group (0 for groups outside the half),
-        // one tensor-memory column per group and half: the epilogue reads them
-        // with the accumulators
-        if (!mbar_wait(smem_u32(&cb.dempty[td]), dph ^ 1u, deadline) && lane == 0) record_timeout(a);
-        tc_fence_after();
-        {
-          uint32_t qv[kQCols];
-#pragma unroll
-          for (int g = 0; g < kQCols; ++g) qv[g] = g < gps ? qsum[g] : 0u;
-          tmem_st4(tmem + lane_addr + C::dbase + td * C::dstride + C::dcols + half * kQCols, qv);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -1077,10 +1067,6 @@ __device__ void dequant_warps(const FusedArgs& a, Ctrl& cb, const int* table, ui
         if (++ta == C::aslots) {
           ta = 0;
           aph ^= 1u;
-        }
-        if (++td == C::dslots) {
-          td = 0;
-          dph ^= 1u;
         }
       }
       if (!keep) {
@@ -1110,7 +1096,7 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
   constexpr int cpg = G / 32, subs = kAccs / (SK / G);
   const uint32_t tmem = cb.tmem;
   int ta = 0, td = 0, xb = 0, g = 0;
-  uint32_t aph = 0, xph = 0;
+  uint32_t aph = 0, dph = 0, xph = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int K = pass == 0 ? a.H : a.I;
@@ -1122,13 +1108,18 @@ __device__ void mma_issuer(const FusedArgs& a, Ctrl& cb, const int* table, uint8
       const uint32_t xbase = smem_u32(xbufs + xb * a.xbuf_bytes);
       for (int s = 0; s < nst; ++s, ++g) {
         const int ta_s = ta, td_s = td;
-        const uint32_t aph_s = aph;
+        const uint32_t aph_s = aph, dph_s = dph;
         if (++ta == C::aslots) {
           ta = 0;
           aph ^= 1u;
         }
-        if (++td == C::dslots) td = 0;
+        if (++td == C::dslots) {
+          td = 0;
+          dph ^= 1u;
+        }
         if ((g & 1) != which) continue;
+        // the accumulator slot's previous stage has been read by the epilogue
+        if (!mbar_wait(smem_u32(&cb.dempty[td_s]), dph_s ^ 1u, deadline)) record_timeout(a);
         if (!mbar_wait(smem_u32(&cb.afull[ta_s]), aph_s, deadline)) record_timeout(a);
         tc_fence_after();
         const uint32_t a_t = tmem + ta_s * C::acols;
@@ -1199,9 +1190,6 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         if (!mbar_wait(smem_u32(&cb.dfull[td]), dph, deadline) && lane == 0) record_timeout(a);
         tc_fence_after();
         const uint32_t dt = tmem + lane_addr + C::dbase + td * C::dstride;
-        uint32_t qh[2][kQCols];
-        tmem_ld4(dt + C::dcols, qh[0]);
-        tmem_ld4(dt + C::dcols + kQCols, qh[1]);
         const uint32_t xs = smem_u32(&meta.xsum[0][0]);
         const uint32_t se = smem_u32(sring + sr * kSRingBytes);
         const bool valid = cb.scale_valid[sr] != 0;
@@ -1224,7 +1212,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         tmem_wait_ld();
 #pragma unroll
         for (int g = 0; g < gps; ++g) {
-          // 256 * D_hi + D_lo' summed over the group's accumulators
+          // 256 * D_hi + D_lo summed over the group's accumulators
           int tsum[kFBM];
 #pragma unroll
           for (int n = 0; n < kFBM; ++n) tsum[n] = 0;
@@ -1236,15 +1224,14 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
           }
           const float sc = scs[g];
           const int z = zs[g];
-          const int q128 = 128 * static_cast<int>(qh[0][g] + qh[1][g]);
           const int gg = s * gps + g;
           const uint4 xa = lds128(xs + gg * kFBM * 4), xb4 = lds128(xs + gg * kFBM * 4 + 16);
           const int xsv[kFBM] = {static_cast<int>(xa.x), static_cast<int>(xa.y), static_cast<int>(xa.z), static_cast<int>(xa.w),
                                  static_cast<int>(xb4.x), static_cast<int>(xb4.y), static_cast<int>(xb4.z), static_cast<int>(xb4.w)};
 #pragma unroll
           for (int n = 0; n < kFBM; ++n) {
-            // sum_k (q - z) v = 256 D_hi + D_lo' + 128 sum q - z sum v
-            const int v = tsum[n] + q128 - z * xsv[n];
+            // sum_k (q - z) v = 256 D_hi + D_lo - z sum v
+            const int v = tsum[n] - z * xsv[n];
             acc[n] = fmaf(static_cast<float>(v), sc, acc[n]);
           }
         }

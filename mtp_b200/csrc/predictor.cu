@@ -10,11 +10,14 @@
 // weight bytes. Weights are prepacked once (mtp_predictor_pack) into the
 // m16n8k16 A-fragment order so that every lane streams its fragments with one
 // 16-byte load per k16 step (a warp reads 512 contiguous bytes). One CTA owns
-// 16 output rows over all of K; its 8 warps split K, and the token columns are
-// processed in chunks of 16 staged in shared memory while the weight
-// fragments stay in registers. The cross-warp sums are reduced in shared
-// memory in a fixed order, then the epilogue adds the bias and either applies
-// SiLU and rounds to bf16 (first linear) or writes fp32 logits (second).
+// 16 output rows over one of KS slices of K (KS chosen so that about 200 or
+// more CTAs stream, two per SM); its 8 warps split the slice, and the token
+// columns are processed in chunks of 16 staged in shared memory while the
+// weight fragments stay in registers. The cross-warp sums are reduced in
+// shared memory in a fixed order and written as fp32 partial slices; the next
+// kernel of the chain adds the slices in slice order, then the bias, and
+// either applies SiLU and rounds to bf16 (the first linear's output, finished
+// while staging) or ranks the fp32 logits (top-k).
 #include "internal.cuh"
 
 namespace mtp {
@@ -24,7 +27,7 @@ namespace {
 constexpr int kPWarps = 8;
 constexpr int kPThreads = kPWarps * 32;
 constexpr int kTokChunk = 16;  // token columns per staged chunk (two n8 tiles)
-constexpr int kMaxKPerWarp = 256;
+constexpr int kMaxKPerWarp = 128;  // 8 weight fragments per lane: two CTAs fit an SM's registers
 
 // mma.sync m16n8k16 bf16 x bf16 -> fp32 (the predictor's weights are plain
 // bf16: no dequantisation, so the register-operand MMA is the direct fit).
@@ -61,7 +64,7 @@ __global__ void pack_kernel(const uint32_t* __restrict__ w, int rows, int cols, 
 // does not depend on scheduling. The input is either bf16 rows x [M][K], or
 // (x == NULL) the previous linear's fp32 partials xin[KSin][M][K], finished
 // on load: bf16(silu(sum + xbias)).
-__global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(kPThreads, 2) gemv_kernel(const uint16_t* __restrict__ x,
                                                          const float* __restrict__ xin, int KSin,
                                                          const uint16_t* __restrict__ xbias, int M, int K,
                                                          const uint4* __restrict__ wp, int R, int KS,
@@ -73,7 +76,7 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
   float* red = reinterpret_cast<float*>(psm + kTokChunk * row_stride);          // [8 warps][16 rows][16 tok]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int strip = blockIdx.x / KS, ks = blockIdx.x % KS;
-  const int kpw = K / KS / kPWarps;  // K per warp (<= 256): kpw / 16 k-steps
+  const int kpw = K / KS / kPWarps;  // K per warp (<= 128): kpw / 16 k-steps
   const int ks0 = (ks * (K / KS)) / 16 + warp * (kpw / 16);
   // Let the next kernel of the chain start streaming its own weights now.
   pdl_launch_dependents();
@@ -98,14 +101,25 @@ __global__ void __launch_bounds__(kPThreads) gemv_kernel(const uint16_t* __restr
         if (x) {
           val = *reinterpret_cast<const uint4*>(x + off);
         } else {
+          // every slice's loads issued together (one L2 round trip), then
+          // summed in slice order
+          float4 p0[kMaxPredictorKs], p1[kMaxPredictorKs];
+#pragma unroll
+          for (int q = 0; q < kMaxPredictorKs; ++q) {
+            if (q < KSin) {
+              p0[q] = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off));
+              p1[q] = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off + 4));
+            }
+          }
           float f[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) f[e] = 0.f;
-          for (int q = 0; q < KSin; ++q) {
-            const float4 p0 = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off));
-            const float4 p1 = __ldcg(reinterpret_cast<const float4*>(xin + q * static_cast<int64_t>(M) * K + off + 4));
-            f[0] += p0.x; f[1] += p0.y; f[2] += p0.z; f[3] += p0.w;
-            f[4] += p1.x; f[5] += p1.y; f[6] += p1.z; f[7] += p1.w;
+#pragma unroll
+          for (int q = 0; q < kMaxPredictorKs; ++q) {
+            if (q < KSin) {
+              f[0] += p0[q].x; f[1] += p0[q].y; f[2] += p0[q].z; f[3] += p0[q].w;
+              f[4] += p1[q].x; f[5] += p1[q].y; f[6] += p1[q].z; f[7] += p1[q].w;
+            }
           }
           uint32_t w[4];
 #pragma unroll
@@ -180,11 +194,22 @@ __global__ void hr_context_kernel(const float* __restrict__ part, int KS, const 
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int c = lane + 32 * j;
-    a[j] = 0.f;
-    if (c < W) {
-      float v = b1 ? __bfloat162float(__ushort_as_bfloat16(b1[c])) : 0.f;
-      for (int q = 0; q < KS; ++q) v += __ldcg(part + (static_cast<int64_t>(q) * M + m) * W + c);
-      a[j] = v / (1.f + expf(-v));
+    a[j] = c < W && b1 ? __bfloat162float(__ushort_as_bfloat16(b1[c])) : 0.f;
+  }
+  // slice by slice, all columns' loads of a slice in flight together
+#pragma unroll
+  for (int q = 0; q < kMaxPredictorKs; ++q) {
+    if (q < KS) {
+      const float* src = part + (static_cast<int64_t>(q) * M + m) * W;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (lane + 32 * j < W) a[j] += __ldcg(src + lane + 32 * j);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (lane + 32 * j < W) {
+      a[j] = a[j] / (1.f + expf(-a[j]));
       sum += a[j];
     }
   }
@@ -214,57 +239,101 @@ __global__ void hr_context_kernel(const float* __restrict__ part, int KS, const 
 // Top-k of each row of E logits (one warp per row; E <= 1024, k <= 32):
 // descending, exact ties to the lower index. The logits are finished here
 // from the second linear's KS partial slices part[ks][m][f * E + i] plus the
-// bias, and written out when `logits` is given.
-__global__ void topk_rows_kernel(const float* __restrict__ part, int KS, const uint16_t* __restrict__ bias,
-                                 int bias_f_stride, int M, int F, int E, int k, float* __restrict__ logits,
-                                 int32_t* __restrict__ ids) {
-  extern __shared__ float tv[];  // [warps][E]
+// bias (bias first, then the slices in order), and written out when `logits`
+// is given. Lane l holds the values l + 32 j (VPL per lane) as order-
+// preserving unsigned keys; each round takes the warp maximum key
+// (redux.sync), the lowest index holding it, and the owning lane recomputes
+// its head.
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t u = __float_as_uint(x + 0.f);  // -0 -> +0: equal values, equal keys
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(128) topk_rows_kernel(const float* __restrict__ part, int KS,
+                                                        const uint16_t* __restrict__ bias, int bias_f_stride, int M,
+                                                        int F, int E, int k, float* __restrict__ logits,
+                                                        int32_t* __restrict__ ids) {
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= M * F) return;
-  float* v = tv + warp * E;
   const int m = row / F, f = row % F;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = lane; i < E; i += 32) {
-    float x = bias ? __bfloat162float(__ushort_as_bfloat16(bias[f * bias_f_stride + i])) : 0.f;
-    for (int q = 0; q < KS; ++q) x += __ldcg(part + (static_cast<int64_t>(q) * M + m) * F * E + f * E + i);
-    v[i] = x;
-    if (logits) logits[static_cast<int64_t>(row) * E + i] = x;
-    if (x > bv) {
-      bv = x;
-      bi = i;
+  const int64_t slice = static_cast<int64_t>(M) * F * E;
+  const float* src = part + static_cast<int64_t>(m) * F * E + static_cast<int64_t>(f) * E;
+  float x[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    x[j] = bias && i < E ? __bfloat162float(__ushort_as_bfloat16(bias[f * bias_f_stride + i])) : 0.f;
+  }
+#pragma unroll
+  for (int q = 0; q < kMaxPredictorKs; ++q) {
+    if (q < KS) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        if (lane + 32 * j < E) x[j] += __ldcg(src + q * slice + lane + 32 * j);
     }
   }
-  __syncwarp();
-  int my_id = -1;
-  for (int j = 0; j < k; ++j) {
-    float wv = bv;
-    int wi = bi;
+  uint32_t key[VPL];  // 0: no value (past E, or taken)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(kFullMask, wv, o);
-      const int oi = __shfl_xor_sync(kFullMask, wi, o);
-      if (ov > wv || (ov == wv && oi < wi)) {
-        wv = ov;
-        wi = oi;
-      }
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    key[j] = i < E ? order_key(x[j]) : 0u;
+    if (logits && i < E) logits[static_cast<int64_t>(row) * E + i] = x[j];
+  }
+  uint32_t hk = 0u;
+  int hj = -1;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j)
+    if (key[j] > hk) {
+      hk = key[j];
+      hj = j;
     }
-    if (lane == j) my_id = wi < E ? wi : -1;
-    if (wi < E && (wi & 31) == lane) {
-      v[wi] = -INFINITY;
-      bv = -INFINITY;
-      bi = 0x7fffffff;
-      for (int i = lane; i < E; i += 32)
-        if (v[i] > bv) {
-          bv = v[i];
-          bi = i;
+  int my_id = -1;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t mk = __reduce_max_sync(kFullMask, hk);
+    const uint32_t cand = hj >= 0 && hk == mk ? static_cast<uint32_t>(lane + 32 * hj) : 0xFFFFFFFFu;
+    const uint32_t wi = __reduce_min_sync(kFullMask, cand);
+    if (lane == r) my_id = mk == 0u ? -1 : static_cast<int>(wi);
+    if (hj >= 0 && static_cast<uint32_t>(lane + 32 * hj) == wi) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        if (j == hj) key[j] = 0u;
+      hk = 0u;
+      hj = -1;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        if (key[j] > hk) {
+          hk = key[j];
+          hj = j;
         }
     }
-    __syncwarp();
   }
   if (lane < k) ids[static_cast<int64_t>(row) * k + lane] = my_id;
+}
+
+int launch_topk_rows(cudaLaunchConfig_t cfg, const float* part, int KS, const uint16_t* bias, int bias_f_stride,
+                     int M, int F, int E, int k, float* logits, int32_t* ids) {
+  const int rows = M * F, wpb = 4;
+  cfg.blockDim = dim3(wpb * 32);
+  cfg.gridDim = dim3((rows + wpb - 1) / wpb);
+  cfg.dynamicSmemBytes = 0;
+  const int vpl = (E + 31) / 32;
+  cudaError_t e;
+  if (vpl <= 1)
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<1>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  else if (vpl <= 2)
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<2>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  else if (vpl <= 4)
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<4>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  else if (vpl <= 8)
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<8>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  else if (vpl <= 16)
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<16>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  else
+    e = cudaLaunchKernelEx(&cfg, topk_rows_kernel<32>, part, KS, bias, bias_f_stride, M, F, E, k, logits, ids);
+  return e == cudaSuccess ? MTP_OK : MTP_ERR_LAUNCH;
 }
 
 size_t gemv_smem(int K) { return static_cast<size_t>(kTokChunk) * (2 * K + 16) + kPWarps * 16 * kTokChunk * 4; }
@@ -279,7 +348,7 @@ int predictor_pack(const uint16_t* w, int rows, int cols, uint16_t* out, cudaStr
 }
 
 // K-splits of one linear (rows R, inner K): enough CTAs to cover the 148 SMs
-// (at least ~200 CTAs), each warp keeping a multiple of 16 of K (at most 256).
+// (at least ~200 CTAs), each warp keeping a multiple of 16 of K (at most 128).
 int predictor_ks(int R, int K) {
   int ks = 1;
   while (ks < kMaxPredictorKs && (R / 16) * ks < 200 && (K / (2 * ks)) % (16 * kPWarps) == 0) ks *= 2;
@@ -325,13 +394,7 @@ int predictor_run(const uint16_t* h, int M, int H, const uint16_t* w1p, const ui
   if (cudaLaunchKernelEx(&cfg, gemv_kernel, static_cast<const uint16_t*>(nullptr), static_cast<const float*>(part1),
                          ks1, b1, M, width, reinterpret_cast<const uint4*>(w2p), R2, ks2, part2) != cudaSuccess)
     return MTP_ERR_LAUNCH;
-  const int rows = M * F, wpb = 4;
-  cfg.blockDim = dim3(wpb * 32);
-  cfg.gridDim = dim3((rows + wpb - 1) / wpb);
-  cfg.dynamicSmemBytes = static_cast<size_t>(wpb) * E * 4;
-  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(part2), ks2, b2, E, M, F, E, k, logits,
-                         ids) != cudaSuccess)
-    return MTP_ERR_LAUNCH;
+  if (launch_topk_rows(cfg, part2, ks2, b2, E, M, F, E, k, logits, ids) != MTP_OK) return MTP_ERR_LAUNCH;
   return launch_status();
 }
 
@@ -385,13 +448,7 @@ int predictor_hr_run(const uint16_t* h, const int32_t* layer_ids, int M, int H, 
                          static_cast<const uint16_t*>(nullptr), M * F, width, reinterpret_cast<const uint4*>(wcp), E,
                          ks2, part2) != cudaSuccess)
     return MTP_ERR_LAUNCH;
-  const int rows = M * F;
-  cfg.blockDim = dim3(wpb * 32);
-  cfg.gridDim = dim3((rows + wpb - 1) / wpb);
-  cfg.dynamicSmemBytes = static_cast<size_t>(wpb) * E * 4;
-  if (cudaLaunchKernelEx(&cfg, topk_rows_kernel, static_cast<const float*>(part2), ks2, bc, 0, M, F, E, k, logits,
-                         ids) != cudaSuccess)
-    return MTP_ERR_LAUNCH;
+  if (launch_topk_rows(cfg, part2, ks2, bc, 0, M, F, E, k, logits, ids) != MTP_OK) return MTP_ERR_LAUNCH;
   return launch_status();
 }
 
