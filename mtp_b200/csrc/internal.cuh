@@ -39,7 +39,7 @@ struct FusedArgs {
   const uint8_t* shared_blob;
   float* gate;               // [M] sigmoid(x . w_g)
   uint8_t* xq;               // [M][xq_row_bytes(H)] quantised x rows, see xq_row_bytes
-  int32_t* bar;              // [8] grid barrier (count, generation),   \ zero before the first
+  int32_t* bar;              // [8] grid-barrier count, (unused),       \ zero before the first
                              //     CTAs done, dirty flag, timeouts seen |
   int32_t* cnt;              // [E] pairs per expert                    |  call; every call
   int32_t* seg_done;         // [max_ws] W1 units published per segment /  leaves them zero

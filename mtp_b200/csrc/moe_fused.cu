@@ -138,7 +138,6 @@ struct Ctrl {
   int seg_first[2];   // first work segment of the pass range
   int cached[2];      // 1 if the pass range's segments are in the table
   int S;              // work segments of this call
-  int gen0;           // grid-barrier generation when the kernel started
   int last;           // 1 in the CTA that finished last
   uint32_t tmem;      // tensor-memory base address
   int scan[32];       // block-scan scratch
@@ -213,11 +212,12 @@ __device__ __forceinline__ void record_timeout(const FusedArgs& a) {
   atomicExch(a.bar + 3, 1);
 }
 
-// The CTA that finishes last (arrival counter bar[2]) checks the dirty flag
-// bar[3]: after a call in which any wait ran out, counters may be left
-// anywhere (a barrier that gave up, late arrivals), so it clears every
-// counter region in full, counts the event in bar[4] and rearms the flag.
-// One timed-out call therefore does not disturb the next.
+// The CTA that finishes last (arrival counter bar[2]) resets the grid-barrier
+// count bar[0] and checks the dirty flag bar[3]: after a call in which any
+// wait ran out, counters may be left anywhere (a barrier that gave up, late
+// arrivals), so it clears every counter region in full, counts the event in
+// bar[4] and rearms the flag. One timed-out call therefore does not disturb
+// the next.
 __device__ void finish_call(const FusedArgs& a, int* last_flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -231,32 +231,30 @@ __device__ void finish_call(const FusedArgs& a, int* last_flag) {
     for (int i = threadIdx.x; i < kMaxWorkSegments; i += blockDim.x) a.seg_done[i] = 0;
     __syncthreads();
     if (threadIdx.x == 0) {
-      a.bar[0] = 0;
       a.bar[4] += 1;
       a.bar[3] = 0;
     }
   }
   if (threadIdx.x == 0) {
+    // every CTA has passed both grid barriers (it arrived here after them)
+    a.bar[0] = 0;
     __threadfence();
     a.bar[2] = 0;
   }
 }
 
-// Grid-wide barrier over the kernel's CTAs (all resident: one per SM). One
-// thread per CTA calls it; the generation word a.bar[1] counts completed
-// barriers, so the kernel waits for `target` = its start value + n. The last
-// arriver clears the arrival count before it publishes the new generation, so
-// the count is zero again for the next barrier and the next call.
-__device__ __forceinline__ bool grid_sync(const FusedArgs& a, int target, uint64_t deadline) {
-  // arrival releases this CTA's writes (ordered before it by the CTA barrier)
-  // and, for the last arriver, acquires everyone else's
-  const int old = atom_acq_rel_gpu_add(a.bar, 1);
-  if (old == static_cast<int>(gridDim.x) - 1) {
-    atomicExch(a.bar, 0);
-    red_release_gpu_add(a.bar + 1, 1);  // ordered after the reset
-    return true;
-  }
-  while (static_cast<int>(static_cast<uint32_t>(ld_acquire_gpu(a.bar + 1)) - static_cast<uint32_t>(target)) < 0) {
+// Grid-wide barrier number n (1, 2) of a call over the kernel's CTAs (all
+// resident: one per SM). One thread per CTA calls it. The arrival count
+// a.bar[0] only grows during a call (the CTA that finishes last sets it back
+// to 0, see finish_call), so barrier n is passed once it reaches n x CTAs.
+// Arrivals are fire-and-forget reductions: no CTA waits for its own atomic's
+// round trip behind the others'.
+__device__ __forceinline__ bool grid_sync(const FusedArgs& a, int n, uint64_t deadline) {
+  // the arrival releases this CTA's writes (ordered before it by the CTA
+  // barrier); the acquiring load that sees the full count acquires everyone's
+  red_release_gpu_add(a.bar, 1);
+  const int target = n * static_cast<int>(gridDim.x);
+  while (ld_acquire_gpu(a.bar) < target) {
     if (global_timer_ns() > deadline) return false;
   }
   return true;
@@ -1317,7 +1315,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     for (int i = 0; i < kSRing; ++i) mbar_init(smem_u32(&cb.sempty[i]), 4);
     mbar_init(smem_u32(&cb.drain), kMmaIssuers);
     fence_mbar_init();
-    cb.gen0 = ld_acquire_gpu(a.bar + 1);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&cb.tmem), kTmemCols);
@@ -1330,7 +1327,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   // Phase 1: route this CTA's tokens (the stage ring is free scratch).
   route_phase(a, reinterpret_cast<float*>(stages));
   __syncthreads();
-  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 1, deadline)) record_timeout(a);
+  if (threadIdx.x == 0 && !grid_sync(a, 1, deadline)) record_timeout(a);
   __syncthreads();
   // Phase 2: the work-segment table of this CTA's unit ranges.
   build_table(a, cb, table, reinterpret_cast<int*>(stages));
@@ -1354,7 +1351,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     tmem_dealloc(cb.tmem, kTmemCols);
   }
   // ------------------------- grid barrier + combine -------------------------
-  if (threadIdx.x == 0 && !grid_sync(a, cb.gen0 + 2, deadline)) record_timeout(a);
+  if (threadIdx.x == 0 && !grid_sync(a, 2, deadline)) record_timeout(a);
   __syncthreads();
   // The per-call counters are no longer read by anyone: zero them for the
   // next call, a slice per CTA.
@@ -1369,25 +1366,40 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   for (int64_t i = b + threadIdx.x; i < e; i += kThreads) {
     const int tok = static_cast<int>(i / quads);
     const int n = static_cast<int>(i % quads) * 4;
+    // every slot's id and y (rows of unrouted slots hold stale values and are
+    // not added) and the shared expert's, loaded together; then the sum in
+    // slot order
+    float gt = 0.f;
+    float4 ys = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.has_shared) {
+      gt = __ldcg(a.gate + tok);
+      ys = ldg_cg_f4(a.ybuf + static_cast<int64_t>(a.numel + tok) * a.H + n);
+    }
     float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < a.k; ++j) {
-      const int pp = tok * a.k + j;
-      const int ex = __ldcg(a.topk_ids + pp);
-      if (ex >= 0 && ex < a.E) {
-        const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(pp) * a.H + n);
-        sum.x += y.x;
-        sum.y += y.y;
-        sum.z += y.z;
-        sum.w += y.w;
+    for (int j0 = 0; j0 < a.k; j0 += 8) {
+      int ex[8];
+      float4 y[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int pp = tok * a.k + j0 + j;
+        ex[j] = j0 + j < a.k ? __ldcg(a.topk_ids + pp) : -1;
+        if (j0 + j < a.k) y[j] = ldg_cg_f4(a.ybuf + static_cast<int64_t>(pp) * a.H + n);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (ex[j] >= 0 && ex[j] < a.E) {
+          sum.x += y[j].x;
+          sum.y += y[j].y;
+          sum.z += y[j].z;
+          sum.w += y[j].w;
+        }
       }
     }
     if (a.has_shared) {
-      const float gt = __ldcg(a.gate + tok);
-      const float4 y = ldg_cg_f4(a.ybuf + static_cast<int64_t>(a.numel + tok) * a.H + n);
-      sum.x = fmaf(gt, y.x, sum.x);
-      sum.y = fmaf(gt, y.y, sum.y);
-      sum.z = fmaf(gt, y.z, sum.z);
-      sum.w = fmaf(gt, y.w, sum.w);
+      sum.x = fmaf(gt, ys.x, sum.x);
+      sum.y = fmaf(gt, ys.y, sum.y);
+      sum.z = fmaf(gt, ys.z, sum.z);
+      sum.w = fmaf(gt, ys.w, sum.w);
     }
     const int64_t o = static_cast<int64_t>(tok) * a.H + n;
     const __nv_bfloat162 lo = __floats2bfloat162_rn(sum.x, sum.y);
