@@ -182,6 +182,19 @@ typedef struct MtpMoeLayerArgs {
                                       again, a call whose waits timed out
                                       included (see _timeouts below)         */
   int64_t workspace_bytes;
+  /* Expert parallelism (ABI version 2). expert_map [global_num_experts], as
+     vLLM fused_experts(expert_map=...) (consumed by the reference at
+     tracing/vllm_wna16_group_plan.py:87-95): topk_ids hold global ids and
+     expert_map[g] is the local expert (index into expert_blobs, below
+     num_experts) or -1 when another rank owns g; such pairs contribute
+     nothing. Only with given ids (router_logits NULL). NULL: ids are local. */
+  const int32_t* expert_map;
+  int32_t global_num_experts;
+  /* Rows [shared_rows_begin, shared_rows_end) get the shared expert (the
+     home rows of an expert-parallel call whose partial rows are summed over
+     ranks); both 0 = every row.                                            */
+  int32_t shared_rows_begin;
+  int32_t shared_rows_end;
 } MtpMoeLayerArgs;
 
 MTP_API int mtp_w4a16_moe_layer_workspace_size(int32_t num_tokens, int32_t num_experts,

@@ -68,6 +68,7 @@ class MtpMoeLayerArgs(C.Structure):
         ("shared_blob", vp), ("shared_gate_weight", vp), ("out", vp), ("out_f32", vp),
         ("topk_weights_out", vp), ("topk_ids_out", vp), ("demand_log", vp), ("status", vp),
         ("workspace", vp), ("workspace_bytes", i64),
+        ("expert_map", vp), ("global_num_experts", i32), ("shared_rows_begin", i32), ("shared_rows_end", i32),
     ]
 
 

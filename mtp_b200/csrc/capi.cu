@@ -83,7 +83,21 @@ const char* mtp_status_string(int status) {
   }
 }
 
-int mtp_abi_version(void) { return 1; }
+int mtp_abi_version(void) { return 2; }
+
+// expert_map / shared-row fields of MtpMoeLayerArgs (ABI version 2)
+static int ep_fields(const MtpMoeLayerArgs& a, int* sh_begin, int* sh_end) {
+  if (a.expert_map) {
+    if (a.router_logits) return MTP_ERR_ARG;
+    if (a.global_num_experts < 1 || a.global_num_experts > 65536) return MTP_ERR_SHAPE;
+  }
+  int b = a.shared_rows_begin, e = a.shared_rows_end;
+  if (b == 0 && e == 0) e = a.num_tokens;
+  if (b < 0 || b > e || e > a.num_tokens) return MTP_ERR_SHAPE;
+  *sh_begin = b;
+  *sh_end = e;
+  return MTP_OK;
+}
 
 int mtp_host_device_pointer(const void* host_ptr, void** device_ptr) {
   if (!host_ptr || !device_ptr) return MTP_ERR_NULL;
@@ -205,6 +219,8 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
       (a.host_blobs && !aligned(a.host_blobs, 256)) ||
       (a.shared_blob && !aligned(a.shared_blob, 256)) || (a.out_f32 && !aligned(a.out_f32, 16)))
     return MTP_ERR_ALIGN;
+  int sh_begin = 0, sh_end = 0;
+  if (const int r = ep_fields(a, &sh_begin, &sh_end)) return r;
   const LayerWs w = layer_ws(M, E, k, H, I);
   if (w.max_ws > kMaxWorkSegments) return MTP_ERR_SHAPE;
   if (a.workspace_bytes < w.total) return MTP_ERR_WORKSPACE;
@@ -225,8 +241,14 @@ int mtp_w4a16_moe_layer(const MtpMoeLayerArgs* p, void* stream) {
     f.topk_ids = a.topk_ids_out ? a.topk_ids_out : reinterpret_cast<int32_t*>(ws + w.tid);
   } else {
     f.topk_w = const_cast<float*>(a.topk_weights);
-    f.topk_ids = const_cast<int32_t*>(a.topk_ids);
+    // mapped ids go to the workspace (the combine phase reads local ids)
+    f.topk_ids = a.expert_map ? reinterpret_cast<int32_t*>(ws + w.tid) : const_cast<int32_t*>(a.topk_ids);
   }
+  f.topk_ids_in = a.router_logits ? f.topk_ids : a.topk_ids;
+  f.emap = a.expert_map;
+  f.E_map = a.expert_map ? a.global_num_experts : 0;
+  f.sh_begin = sh_begin;
+  f.sh_end = sh_end;
   f.wseg = reinterpret_cast<int32_t*>(ws + w.wseg);
   f.L = L;
   f.blobs = a.expert_blobs; f.expert_bytes = a.expert_bytes;
@@ -309,6 +331,8 @@ int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* p, void* stream) {
       !aligned(a.expert_blobs, 256) || (a.expert_bytes % 256) || (a.shared_blob && !aligned(a.shared_blob, 256)) ||
       (a.shared_gate_weight && !aligned(a.shared_gate_weight, 16)) || (a.out_f32 && !aligned(a.out_f32, 16)))
     return MTP_ERR_ALIGN;
+  int sh_begin = 0, sh_end = 0;
+  if (const int r = ep_fields(a, &sh_begin, &sh_end)) return r;
   const PrefillWs w = prefill_ws(M, E, k, H, I, has_shared);
   if (a.workspace_bytes < w.total) return MTP_ERR_WORKSPACE;
 
@@ -325,6 +349,10 @@ int mtp_w4a16_moe_prefill(const MtpMoeLayerArgs* p, void* stream) {
     f.topk_w = a.topk_weights;
     f.topk_ids = a.topk_ids;
   }
+  f.emap = a.expert_map;
+  f.E_map = a.expert_map ? a.global_num_experts : 0;
+  f.sh_begin = sh_begin;
+  f.sh_end = sh_end;
   f.ids_x = reinterpret_cast<int32_t*>(ws + w.ids_x);
   f.w_x = reinterpret_cast<float*>(ws + w.w_x);
   f.inv = reinterpret_cast<int32_t*>(ws + w.inv);

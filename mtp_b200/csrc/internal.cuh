@@ -29,7 +29,11 @@ struct FusedArgs {
   const float* logits;       // [M, E] or NULL (topk_w / topk_ids given)
   const uint16_t* gate_w;    // [H] shared-expert gate or NULL
   float* topk_w;             // [M*k] written when logits != NULL
-  int32_t* topk_ids;         // [M*k]
+  int32_t* topk_ids;         // [M*k] local ids (written when logits != NULL or emap != NULL)
+  const int32_t* topk_ids_in;  // [M*k] the caller's ids (global when emap != NULL)
+  const int32_t* emap;       // [E_map] global -> local expert or -1; NULL: ids are local
+  int E_map;
+  int sh_begin, sh_end;      // rows that get the shared expert
   int32_t* wseg;             // [max_ws][kWsInts] spill area for large ranges
   MtpExpertLayout L;
   const uint8_t* blobs;
@@ -94,7 +98,10 @@ struct PrefillArgs {
   const uint16_t* x;           // [M, H] bf16
   const uint16_t* gate_w;      // [H] bf16 shared-expert gate or NULL
   const float* topk_w;         // [M, k]
-  const int32_t* topk_ids;     // [M, k]
+  const int32_t* topk_ids;     // [M, k] (global ids when emap != NULL)
+  const int32_t* emap;         // [E_map] global -> local expert or -1; NULL: ids are local
+  int E_map;
+  int sh_begin, sh_end;        // rows that get the shared expert
   int32_t* ids_x;              // [M, kx] pairs extended by the shared expert (id E)
   float* w_x;                  // [M, kx] pair weights (sigmoid gate for the shared expert)
   int32_t* inv;                // [M, kx] sorted position of each pair, -1 if not routed

@@ -522,8 +522,15 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
           a.topk_ids[t * a.k + lane] = id;
         }
       } else if (lane < a.k) {
-        id = a.topk_ids[t * a.k + lane];
+        // caller-given ids; global ones go through the expert map (-1: the
+        // pair belongs to another rank) and the local ids are kept for the
+        // combine phase
+        id = a.topk_ids_in[t * a.k + lane];
         w = a.topk_w[t * a.k + lane];
+        if (a.emap) {
+          id = id >= 0 && id < a.E_map ? a.emap[id] : -1;
+          a.topk_ids[t * a.k + lane] = id;
+        }
       }
       // the pair's combine weight travels with its gate|up row to the W2 pass
       if (lane < a.k) a.gu[static_cast<int64_t>(t * a.k + lane) * gu_stride(a) + 2 * a.I] = w;
@@ -548,7 +555,7 @@ __device__ void route_phase(const FusedArgs& a, float* scratch) {
         if (a.has_shared && lane + 32 * j < nvec) wv[j] = __ldg(wg + lane + 32 * j);
       }
       quantize_token(a, t, xv);
-      if (a.has_shared) {
+      if (a.has_shared && t >= a.sh_begin && t < a.sh_end) {
         float part = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -583,8 +590,8 @@ __device__ void fill_entry(const FusedArgs& a, int s, int shared_ws, const int* 
     blob = a.shared_blob;
     flags = 1;
     for (int j = 0; j < kFBM; ++j) {
-      const int tk = s * kFBM + j;
-      w[4 + j] = tk < a.M ? a.numel + tk : -1;
+      const int tk = a.sh_begin + s * kFBM + j;
+      w[4 + j] = tk < a.sh_end ? a.numel + tk : -1;
     }
   } else {
     const int r = s - shared_ws;
@@ -645,7 +652,7 @@ __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scrat
     }
   }
   if (tid == 0) sbase[a.E] = total;
-  const int shared_ws = a.has_shared ? (a.M + kFBM - 1) / kFBM : 0;
+  const int shared_ws = a.has_shared ? (a.sh_end - a.sh_begin + kFBM - 1) / kFBM : 0;
   const int S = shared_ws + total;
   if (tid == 0) cb.S = S;
   if (blockIdx.x == 0) {
@@ -1369,9 +1376,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     // every slot's id and y (rows of unrouted slots hold stale values and are
     // not added) and the shared expert's, loaded together; then the sum in
     // slot order
+    const bool with_shared = a.has_shared && tok >= a.sh_begin && tok < a.sh_end;
     float gt = 0.f;
     float4 ys = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (a.has_shared) {
+    if (with_shared) {
       gt = __ldcg(a.gate + tok);
       ys = ldg_cg_f4(a.ybuf + static_cast<int64_t>(a.numel + tok) * a.H + n);
     }
@@ -1395,7 +1403,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
         }
       }
     }
-    if (a.has_shared) {
+    if (with_shared) {
       sum.x = fmaf(gt, ys.x, sum.x);
       sum.y = fmaf(gt, ys.y, sum.y);
       sum.z = fmaf(gt, ys.z, sum.z);

@@ -123,7 +123,9 @@ __device__ __forceinline__ void dequant_word_bf16(uint32_t w, __nv_bfloat162 zb,
 }
 
 // ---------------------------------------------------------------------------
-// prep: pair lists extended by the shared expert, inverse map reset
+// prep: pair lists (global ids through the expert map when one is given)
+// extended by the shared expert for the rows in [sh_begin, sh_end), inverse
+// map reset
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,12 +133,20 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillArgs a) 
   if (t >= a.M) return;
   for (int j = lane; j < a.k; j += 32) {
     const int64_t src = static_cast<int64_t>(t) * a.k + j, dst = static_cast<int64_t>(t) * a.kx + j;
-    const int id = a.topk_ids[src];
+    int id = a.topk_ids[src];
+    if (a.emap) id = id >= 0 && id < a.E_map ? a.emap[id] : -1;
     a.ids_x[dst] = id >= 0 && id < a.E ? id : -1;
     a.w_x[dst] = a.topk_w[src];
     a.inv[dst] = -1;
   }
-  if (a.has_shared) {
+  if (a.has_shared && (t < a.sh_begin || t >= a.sh_end)) {
+    if (lane == 0) {
+      const int64_t dst = static_cast<int64_t>(t) * a.kx + a.k;
+      a.ids_x[dst] = -1;
+      a.w_x[dst] = 0.f;
+      a.inv[dst] = -1;
+    }
+  } else if (a.has_shared) {
     const uint4* xr = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(t) * a.H);
     const uint4* wg = reinterpret_cast<const uint4*>(a.gate_w);
     float part = 0.f;

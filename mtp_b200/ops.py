@@ -243,7 +243,9 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
                     out: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,
                     topk_out: tuple[torch.Tensor, torch.Tensor] | None = None,
                     demand_log: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                    workspace: torch.Tensor | None = None, path: str = "auto") -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, path: str = "auto",
+                    expert_map: torch.Tensor | None = None,
+                    shared_rows: tuple[int, int] | None = None) -> torch.Tensor:
     """One W4A16 MoE layer forward: router (when ``router_logits`` is given,
     else the given ``topk_weights``/``topk_ids``), align, gate_up + SiLU*up,
     down + routed weight, top-k sum and the sigmoid-gated shared expert.
@@ -256,7 +258,12 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     ``path``: "decode" (the persistent layer kernel), "prefill" (128-pair
     bf16 tiles; every expert resident, no ``slot_table`` / ``demand_log``) or
     "auto": prefill when :func:`layer_path` says so, the call allows it and a
-    given ``workspace`` is large enough for it."""
+    given ``workspace`` is large enough for it.
+
+    Expert parallelism: ``expert_map`` [global E] int32 (vLLM's expert_map)
+    takes global ``topk_ids`` to this shard's experts (-1: another rank's,
+    the pair contributes nothing); ``shared_rows`` = (begin, end) restricts
+    the shared expert to those rows."""
     _check_cuda("hidden_states", hidden_states, torch.bfloat16, 2)
     m, h = hidden_states.shape
     if h != experts.hidden:
@@ -330,6 +337,19 @@ def moe_layer_w4a16(hidden_states: torch.Tensor, router_logits: torch.Tensor | N
     args.status = status.data_ptr() if status is not None else None
     args.workspace = workspace.data_ptr()
     args.workspace_bytes = workspace.numel()
+    if expert_map is not None:
+        if router_logits is not None:
+            raise ValueError("expert_map needs given topk_ids (global ids), not router_logits")
+        _check_cuda("expert_map", expert_map, torch.int32, 1)
+        args.expert_map = expert_map.data_ptr()
+        args.global_num_experts = expert_map.numel()
+    if shared_rows is not None:
+        b, e_ = int(shared_rows[0]), int(shared_rows[1])
+        if not 0 <= b <= e_ <= m:
+            raise ValueError(f"shared_rows {shared_rows} outside [0, {m}]")
+        if b == e_:
+            raise ValueError("an empty shared_rows range: pass shared=None instead")
+        args.shared_rows_begin, args.shared_rows_end = b, e_
     _lib.call("mtp_w4a16_moe_prefill" if path == "prefill" else "mtp_w4a16_moe_layer", C.byref(args),
               _stream(hidden_states))
     return out

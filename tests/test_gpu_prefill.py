@@ -188,3 +188,41 @@ def test_prefill_shared_expert_only_call(cuda_device):
     o = olayer.MoeLayerOracle(experts, sh)
     ref = o.moe_tokens(x.float(), torch.zeros((300, 2), dtype=torch.long), torch.zeros((300, 2)))
     check(out, ref)
+
+
+@pytest.mark.parametrize("path", ["decode", "prefill"])
+def test_expert_map_and_shared_rows(cuda_device, path):
+    """The expert-parallel fields of the layer call: global ids through an
+    expert_map (this shard = global experts 8-15 of 16) give the same bits as
+    the ids masked by hand; the shared expert restricted to rows [b, e) adds
+    exactly the shared-only call's output on those rows (within the bf16
+    bound) and nothing elsewhere."""
+    import mtp_b200
+    from mtp_b200.synthetic import LayerConfig, make_inputs, make_layer
+    m = 300 if path == "prefill" else 40
+    cfg = LayerConfig(num_experts=8, hidden=512, inter=256, top_k=4, shared=True, tokens=(m,))
+    experts, sh = make_layer(cfg, seed=71)
+    w, s = build(experts, sh, cuda_device)
+    x, _ = make_inputs(cfg, m, seed=72)
+    x = x.to(cuda_device)
+    g = torch.Generator().manual_seed(73)
+    gids = torch.stack([torch.randperm(16, generator=g)[:4] for _ in range(m)]).to(torch.int32)
+    gw = torch.rand((m, 4), generator=g)
+    emap = torch.full((16,), -1, dtype=torch.int32)
+    emap[8:] = torch.arange(8, dtype=torch.int32)
+    lids = torch.where(gids >= 8, gids - 8, torch.full_like(gids, -1))
+    lw = torch.where(gids >= 8, gw, torch.zeros(()))
+    gids, gw, lids, lw, emap = (t.to(cuda_device) for t in (gids, gw, lids, lw, emap))
+    a = mtp_b200.moe_layer_w4a16(x, None, w, 4, topk_weights=gw, topk_ids=gids, expert_map=emap, path=path)
+    b = mtp_b200.moe_layer_w4a16(x, None, w, 4, topk_weights=lw, topk_ids=lids, path=path)
+    assert torch.equal(a, b)
+    r0, r1 = m // 4, m // 2
+    c = mtp_b200.moe_layer_w4a16(x, None, w, 4, shared=s, topk_weights=gw, topk_ids=gids, expert_map=emap,
+                                 shared_rows=(r0, r1), path=path)
+    assert torch.equal(c[:r0], b[:r0]) and torch.equal(c[r1:], b[r1:])
+    none_ids = torch.full((m, 4), -1, dtype=torch.int32, device=cuda_device)
+    only = mtp_b200.moe_layer_w4a16(x, None, w, 4, shared=s, topk_weights=torch.zeros((m, 4), device=cuda_device),
+                                    topk_ids=none_ids, path=path)
+    check(c[r0:r1], (b[r0:r1].float() + only[r0:r1].float()).cpu())
+    with pytest.raises(ValueError):
+        mtp_b200.moe_layer_w4a16(x, torch.zeros((m, 8), device=cuda_device), w, 4, expert_map=emap, path=path)
