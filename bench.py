@@ -305,16 +305,22 @@ def run_gpu(args, rank: int, world: int):
     total_bytes = sum(bytes_per_m.values())
     total_ms = sum(per_m_ms.values())
     achieved = total_bytes / (total_ms / 1e3) / 1e9
-    # DRAM traffic per launch: the ncu-measured traffic/algorithmic ratio of
-    # the layer kernel (profiles/traffic.json, one capture at M=16) applied to
-    # this run's average algorithmic bytes per launch
+    # DRAM traffic per launch: the ncu-measured traffic/algorithmic ratios of
+    # the layer kernel (profiles/traffic.json, one capture per listed M),
+    # each sweep point taking the capture nearest in log2(M), applied to this
+    # run's algorithmic bytes and averaged over the launches
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     n_launch = len(sweep) * args.layers
     if tp.exists():
-        ratio = json.loads(tp.read_text()).get("traffic_over_algorithmic")
-        if ratio:
-            traffic = round(ratio * total_bytes / n_launch)
+        caps = [(c["M"], c["traffic_over_algorithmic"]) for c in json.loads(tp.read_text()).get("captures", [])]
+        if caps:
+            import math
+
+            def ratio_for(m):
+                return min(caps, key=lambda c: (abs(math.log2(c[0]) - math.log2(m)), -c[0]))[1]
+
+            traffic = round(sum(ratio_for(m) * bytes_per_m[m] for m in sweep) / n_launch)
 
     # end to end through the public API with host buffers (pinned), copies timed
     e2e = run_e2e(args, layers, cfg, sweep, dev, state) if not args.no_e2e else None
