@@ -138,6 +138,29 @@ def test_layer_is_deterministic(cuda_device, config1):
     assert torch.equal(a, b)
 
 
+def test_workspace_counters_clean_after_calls(cuda_device, config1):
+    """Calls of different sizes on one workspace: no wait ran out (the
+    timeout count stays 0) and the fixed counter region is zero again after
+    every call, so the next call of any size starts clean."""
+    import ctypes
+
+    import mtp_b200
+    from mtp_b200 import _lib
+    from mtp_b200.synthetic import CONFIG1, make_inputs
+    _, _, w, s = config1
+    ws = mtp_b200.layer_workspace(64, w, 8, cuda_device)
+    for m in (64, 1, 17, 64):
+        x, logits = make_inputs(CONFIG1, m, seed=m, device=cuda_device)
+        mtp_b200.moe_layer_w4a16(x, logits, w, 8, shared=s, workspace=ws)
+        torch.cuda.synchronize()
+        # bar [8] at 0, cnt [1024] at 256, seg_done [32768] at 4352 (256-byte aligned regions)
+        counters = ws[:4352 + 4 * 32768].view(torch.int32)
+        assert int(counters.count_nonzero()) == 0, f"M={m}: counters left non-zero"
+    n = ctypes.c_int32(-1)
+    _lib.call("mtp_w4a16_moe_layer_timeouts", ws.data_ptr(), ctypes.byref(n), None)
+    assert n.value == 0
+
+
 def test_slot_table_and_host_store_are_bit_identical(cuda_device, config1):
     """Premap indirection: a 64-slot cache holding a permuted subset of the
     experts; the others are served from pinned host memory (demand fetch)."""
