@@ -147,7 +147,6 @@ static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
 // Per operand buffer: quantisation metadata of its 8 rows.
 struct OperandMeta {
   float sx[kFBM];                // row scale: x = sx * (256 * hi + lo)
-  float amax[kDQ][kFBM];         // per-warp row maxima (scratch)
   int xsum[kMaxGroups][kFBM];    // per quantisation group and row: sum of the 16-bit values
 };
 
@@ -938,68 +937,70 @@ __device__ __forceinline__ void relayout_x_rows(const FusedArgs& a, const int* p
 // W2 operand: the 8 pair rows arrive as fp32 W1 sums (K gate values, K up
 // values, the combine weight, padding); form h = bf16(silu(gate) * up) and
 // quantise it in place to 16-bit integers v = 256 * hi + lo (pack_hilo), laid
-// out as the B planes above, with one scale per row (times the combine weight)
-// and per-group sums of v. Thread (warp w, lane = 4n + q) owns
-// the 4-element groups k = 16 cc + 4q of row n for cc = w + 8i.
+// out as the B planes above, with one scale per row (times the combine
+// weight) and per-group sums of v. Dequant warp n owns row n: lane l takes
+// the 16-element chunks c = l + 32 i of K, so the row maximum and the group
+// sums are warp shuffles. Every warp holds its row in registers before the
+// barrier, after which the planes overwrite the rows in place.
+static_assert(kDQ == kFBM, "one dequant warp per operand row");
+
 template <int G>
 __device__ __forceinline__ void quantize_h_rows(uint8_t* rows, OperandMeta& meta, int K) {
-  const int t = threadIdx.x, w = t >> 5, lane = t & 31, n = lane >> 2, q = lane & 3;
-  const int iters = K / 128;  // <= 8
+  const int n = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunks = K / 16;  // <= 64: at most two per lane
   const uint8_t* row = rows + n * (8 * K + 16);
-  uint2 raw[8];
+  uint32_t hv[2][8];           // bf16 pairs of the lane's chunks
   float mx = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    raw[i] = make_uint2(0u, 0u);
-    if (i < iters) {
-      const int k0 = 16 * (w + 8 * i) + 4 * q;
-      const float4 g = *reinterpret_cast<const float4*>(row + 4 * k0);
-      const float4 u = *reinterpret_cast<const float4*>(row + 4 * (K + k0));
-      const __nv_bfloat162 h01 = __floats2bfloat162_rn(silu_fast(g.x) * u.x, silu_fast(g.y) * u.y);
-      const __nv_bfloat162 h23 = __floats2bfloat162_rn(silu_fast(g.z) * u.z, silu_fast(g.w) * u.w);
-      raw[i].x = *reinterpret_cast<const uint32_t*>(&h01);
-      raw[i].y = *reinterpret_cast<const uint32_t*>(&h23);
-      const uint32_t m0 = __vmaxu2(raw[i].x & 0x7fff7fffu, raw[i].y & 0x7fff7fffu);
-      mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
+  for (int it = 0; it < 2; ++it) {
+    const int c = lane + 32 * it;
+    if (c < nchunks) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k0 = 16 * c + 4 * q;
+        const float4 g = *reinterpret_cast<const float4*>(row + 4 * k0);
+        const float4 u = *reinterpret_cast<const float4*>(row + 4 * (K + k0));
+        const __nv_bfloat162 h01 = __floats2bfloat162_rn(silu_fast(g.x) * u.x, silu_fast(g.y) * u.y);
+        const __nv_bfloat162 h23 = __floats2bfloat162_rn(silu_fast(g.z) * u.z, silu_fast(g.w) * u.w);
+        hv[it][2 * q] = *reinterpret_cast<const uint32_t*>(&h01);
+        hv[it][2 * q + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+        const uint32_t m0 = __vmaxu2(hv[it][2 * q] & 0x7fff7fffu, hv[it][2 * q + 1] & 0x7fff7fffu);
+        mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m0 & 0xffff0000u)));
+      }
     }
   }
-  mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 1));
-  mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 2));
-  if (q == 0) meta.amax[w][n] = mx;
-  for (int i = t; i < kFBM * kMaxGroups; i += kDQ * 32) (&meta.xsum[0][0])[i] = 0;
+  mx = warp_max(mx);
   // the pair's combine weight (top-k weight, 1 for the shared expert) rides in
   // the row tail; read before the planes overwrite it, folded into the scale
-  float cw = 0.f;
-  if (t < kFBM) cw = *reinterpret_cast<const float*>(rows + t * (8 * K + 16) + 8 * K);
+  const float cw = *reinterpret_cast<const float*>(row + 8 * K);
   named_bar_sync(kBarDequant, kDQ * 32);
-  float amax = 0.f;
+  const float inv = mx > 0.f ? kVMax / mx : 0.f;
+  constexpr int cpg = G / 16;  // chunks per quantisation group: 4 or 8 consecutive lanes
 #pragma unroll
-  for (int j = 0; j < kDQ; ++j) amax = fmaxf(amax, meta.amax[j][n]);
-  const float inv = amax > 0.f ? kVMax / amax : 0.f;
+  for (int it = 0; it < 2; ++it) {
+    const int c = lane + 32 * it;
+    int sum = 0;
+    if (c < nchunks) {
+      uint32_t hw[4], lw[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < iters) {  // warp-uniform
-      const int cc = w + 8 * i;
-      const int v0 = __float2int_rn(__uint_as_float(raw[i].x << 16) * inv);
-      const int v1 = __float2int_rn(__uint_as_float(raw[i].x & 0xffff0000u) * inv);
-      const int v2 = __float2int_rn(__uint_as_float(raw[i].y << 16) * inv);
-      const int v3 = __float2int_rn(__uint_as_float(raw[i].y & 0xffff0000u) * inv);
-      uint32_t hw, lw;
-      pack_hilo(v0, v1, v2, v3, hw, lw);
-      const int off = cc * 128 + n * 16 + 4 * q;
-      *reinterpret_cast<uint32_t*>(rows + off) = hw;
-      *reinterpret_cast<uint32_t*>(rows + 8 * K + off) = lw;
-      int sum = v0 + v1 + v2 + v3;
-      sum += __shfl_xor_sync(kFullMask, sum, 1);
-      sum += __shfl_xor_sync(kFullMask, sum, 2);
-      if (q == 0) atomicAdd(&meta.xsum[(16 * cc) / G][n], sum);
+      for (int q = 0; q < 4; ++q) {
+        const int v0 = __float2int_rn(__uint_as_float(hv[it][2 * q] << 16) * inv);
+        const int v1 = __float2int_rn(__uint_as_float(hv[it][2 * q] & 0xffff0000u) * inv);
+        const int v2 = __float2int_rn(__uint_as_float(hv[it][2 * q + 1] << 16) * inv);
+        const int v3 = __float2int_rn(__uint_as_float(hv[it][2 * q + 1] & 0xffff0000u) * inv);
+        pack_hilo(v0, v1, v2, v3, hw[q], lw[q]);
+        sum += v0 + v1 + v2 + v3;
+      }
+      const int off = c * 128 + n * 16;
+      *reinterpret_cast<uint4*>(rows + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(rows + 8 * K + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
+    // the group's chunks are cpg consecutive lanes of one pass
+#pragma unroll
+    for (int o = 1; o < cpg; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
+    if (c < nchunks && (lane & (cpg - 1)) == 0) meta.xsum[(16 * c) / G][n] = sum;
   }
-  if (t < kFBM) {
-    float m = 0.f;
-    for (int j = 0; j < kDQ; ++j) m = fmaxf(m, meta.amax[j][t]);
-    meta.sx[t] = m / kVMax * cw;
-  }
+  if (lane == 0) meta.sx[n] = mx / kVMax * cw;
   fence_proxy_async_shared();  // the plane stores are read by the tensor cores
   named_bar_sync(kBarDequant, kDQ * 32);
 }
