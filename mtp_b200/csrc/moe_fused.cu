@@ -1329,9 +1329,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
     tmem_relinquish();
   }
   const uint64_t deadline = global_timer_ns() + kTimeoutNs;
+  // Launched with programmatic stream serialisation: the next kernel in the
+  // stream may be scheduled onto an SM as soon as this CTA leaves it (its
+  // prologue above overlaps this call's tail), and this call reads nothing in
+  // global memory before the previous kernel has finished.
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
   // Phase 1: route this CTA's tokens (the stage ring is free scratch).
   route_phase(a, reinterpret_cast<float*>(stages));
   __syncthreads();
@@ -1514,11 +1520,13 @@ static int launch_fused_t(const FusedArgs& a, const FusedGeometry& f, cudaStream
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = f.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, moe_fused_kernel<SK, G>, a) != cudaSuccess) {
     cudaGetLastError();
     return MTP_ERR_LAUNCH;
