@@ -197,11 +197,11 @@ __device__ __forceinline__ Pass make_pass(const FusedArgs& a, const Ctrl& cb, co
 
 
 // A unit reuses the operand buffer of the previous unit when both belong to
-// the same single-block segment (same rows).
+// the same segment (one token block: the same operand rows). A plain index
+// test: a table read here sat on every role's per-unit path.
+static_assert(kWsBlocks == 1, "a work segment is one token block");
 __device__ __forceinline__ bool reuses_operand(const Pass& P, int u) {
-  if (u == P.ub) return false;
-  const int s = u / P.per;
-  return s == (u - 1) / P.per && ws_entry(P, s)[2] == 1;
+  return u != P.ub && u / P.per == (u - 1) / P.per;
 }
 
 // A wait ran out: report it (status bit 0) and mark the workspace so that the
@@ -1249,7 +1249,12 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
           dph ^= 1u;
         }
       }
-      const int* cols = e + 4;
+      // the pair columns and row scales loaded together (16-byte loads) before
+      // the stores, so the loads do not wait behind each store
+      const int4 cq0 = *reinterpret_cast<const int4*>(e + 4), cq1 = *reinterpret_cast<const int4*>(e + 8);
+      const float4 sq0 = *reinterpret_cast<const float4*>(&meta.sx[0]), sq1 = *reinterpret_cast<const float4*>(&meta.sx[4]);
+      const int cols[kFBM] = {cq0.x, cq0.y, cq0.z, cq0.w, cq1.x, cq1.y, cq1.z, cq1.w};
+      const float sxv[kFBM] = {sq0.x, sq0.y, sq0.z, sq0.w, sq1.x, sq1.y, sq1.z, sq1.w};
       if (pass == 0) {
         // gate rows 0-63 and up rows 64-127 of block b: fp32 sums per pair;
         // silu(gate) * up is formed when the W2 operand is loaded
@@ -1257,7 +1262,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
 #pragma unroll
         for (int n = 0; n < kFBM; ++n) {
           const int p = cols[n];
-          if (p >= 0) a.gu[static_cast<int64_t>(p) * gu_stride(a) + row] = acc[n] * meta.sx[n];
+          if (p >= 0) a.gu[static_cast<int64_t>(p) * gu_stride(a) + row] = acc[n] * sxv[n];
         }
         ++published;
         if (u + 1 == P.ue || (u + 1) / P.per != seg) {
@@ -1271,7 +1276,7 @@ __device__ void epilogue_warps(const FusedArgs& a, Ctrl& cb, const int* table, c
         for (int n = 0; n < kFBM; ++n) {
           const int p = cols[n];
           if (p >= 0) {
-            a.ybuf[static_cast<int64_t>(p) * a.H + 128 * b + r] = acc[n] * meta.sx[n];
+            a.ybuf[static_cast<int64_t>(p) * a.H + 128 * b + r] = acc[n] * sxv[n];
           }
         }
       }
