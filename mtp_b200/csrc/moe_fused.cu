@@ -742,25 +742,13 @@ __device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
 // producers
 // ---------------------------------------------------------------------------
 // Stage s of unit (pass, row block b): K range [s * SK, (s + 1) * SK) of the
-// block, three contiguous byte ranges of the blob.
+// block, three contiguous byte ranges of the blob (int4 words, group scales,
+// zero points).
 struct Piece {
   uint32_t src_off;
   uint32_t dst_off;
   uint32_t bytes;
 };
-
-__device__ __forceinline__ void stage_pieces(const FusedArgs& a, int pass, int b, int s, Piece* p) {
-  const int K = pass == 0 ? a.H : a.I;
-  const uint32_t q0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_qweight : a.L.w2_qweight);
-  const uint32_t s0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_scales : a.L.w2_scales);
-  const uint32_t z0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_zeros : a.L.w2_zeros);
-  const uint32_t chunk = static_cast<uint32_t>(b) * (K / 32) + static_cast<uint32_t>(s) * (a.sk / 32);
-  const uint32_t grp = static_cast<uint32_t>(b) * (K / a.G) + static_cast<uint32_t>(s) * (a.sk / a.G);
-  const uint32_t wb = static_cast<uint32_t>(a.sk) * 64u, sb = (a.sk / a.G) * 256u, zb = (a.sk / a.G) * 64u;
-  p[0] = {q0 + chunk * 2048u, 0u, wb};
-  p[1] = {s0 + grp * 256u, wb, sb};
-  p[2] = {z0 + grp * 64u, wb + sb, zb};
-}
 
 // Each stage: the int4 words into the weight ring (read and released by the
 // dequant warps), the group scales and zero points into the scale ring (read
@@ -774,13 +762,25 @@ __device__ void weight_producer(const FusedArgs& a, Ctrl& cb, const int* table, 
   for (int pass = 0; pass < 2; ++pass) {
     const Pass P = make_pass(a, cb, table, pass);
     const int nst = (pass == 0 ? a.H : a.I) / a.sk;
+    // the pass's piece geometry, computed once per pass: a stage's pieces
+    // then cost two multiply-adds (no division on the producer's path)
+    const int Kp = pass == 0 ? a.H : a.I;
+    const uint32_t q0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_qweight : a.L.w2_qweight);
+    const uint32_t s0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_scales : a.L.w2_scales);
+    const uint32_t z0 = static_cast<uint32_t>(pass == 0 ? a.L.w13_zeros : a.L.w2_zeros);
+    const uint32_t kb = Kp / 32, ks = a.sk / 32, gb = Kp / a.G, gsk = a.sk / a.G;
+    const uint32_t wbytes = static_cast<uint32_t>(a.sk) * 64u, sbytes = gsk * 256u, zbytes = gsk * 64u;
     for (int u = P.ub, seg = P.ub / P.per, b = P.ub % P.per; u < P.ue; ++u, next_unit(P, seg, b)) {
       const int* e = ws_entry(P, seg);
       const uint8_t* blob = ws_blob(e);
       const bool host = (e[3] & 2) != 0;
       for (int s = 0; s < nst; ++s) {
         Piece pc[3];
-        stage_pieces(a, pass, b, s, pc);
+        const uint32_t chunk = static_cast<uint32_t>(b) * kb + static_cast<uint32_t>(s) * ks;
+        const uint32_t grp = static_cast<uint32_t>(b) * gb + static_cast<uint32_t>(s) * gsk;
+        pc[0] = {q0 + chunk * 2048u, 0u, wbytes};
+        pc[1] = {s0 + grp * 256u, wbytes, sbytes};
+        pc[2] = {z0 + grp * 64u, wbytes + sbytes, zbytes};
         if (!mbar_wait(smem_u32(&cb.empty[st]), ph ^ 1u, deadline) && lane == 0) record_timeout(a);
         if (!mbar_wait(smem_u32(&cb.sempty[sr]), sph ^ 1u, deadline) && lane == 0) record_timeout(a);
         uint8_t* dst[3];
@@ -1387,9 +1387,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   const int quads = a.H / 4;
   const int64_t total = static_cast<int64_t>(a.M) * quads;
   const int64_t b = total * blockIdx.x / gridDim.x, e = total * (blockIdx.x + 1) / gridDim.x;
-  for (int64_t i = b + threadIdx.x; i < e; i += kThreads) {
-    const int tok = static_cast<int>(i / quads);
-    const int n = static_cast<int>(i % quads) * 4;
+  // (token, quad) of element i carried along, one division per thread
+  int ctok = static_cast<int>((b + threadIdx.x) / quads), cq = static_cast<int>((b + threadIdx.x) % quads);
+  const int dtok = kThreads / quads, dq = kThreads % quads;
+  for (int64_t i = b + threadIdx.x; i < e; i += kThreads, ctok += dtok, cq += dq, ctok += cq >= quads, cq -= cq >= quads ? quads : 0) {
+    const int tok = ctok;
+    const int n = cq * 4;
     // every slot's id and y (rows of unrouted slots hold stale values and are
     // not added) and the shared expert's, loaded together; then the sum in
     // slot order
