@@ -137,6 +137,7 @@ struct Ctrl {
   int scale_valid[kSRing];      // 0: the stage's expert has no weights (its terms are zero)
   int seg_first[2];   // first work segment of the pass range
   int cached[2];      // 1 if the pass range's segments are in the table
+  int ub[2], ue[2];   // this CTA's unit range per pass
   int S;              // work segments of this call
   int last;           // 1 in the CTA that finished last
   uint32_t tmem;      // tensor-memory base address
@@ -180,16 +181,21 @@ __device__ __forceinline__ int pair_token(const FusedArgs& a, int p) {
 }
 
 __device__ __forceinline__ void unit_range(int total_units, int& b, int& e) {
-  const int64_t g = gridDim.x, c = blockIdx.x;
-  b = static_cast<int>(total_units * c / g);
-  e = static_cast<int>(total_units * (c + 1) / g);
+  const uint32_t g = gridDim.x, c = blockIdx.x, t = static_cast<uint32_t>(total_units);
+  if (t <= 0xffffffffu / g) {  // 32-bit products: the common case, no 64-bit division
+    b = static_cast<int>(t * c / g);
+    e = static_cast<int>(t * (c + 1) / g);
+  } else {
+    b = static_cast<int>(static_cast<uint64_t>(t) * c / g);
+    e = static_cast<int>(static_cast<uint64_t>(t) * (c + 1) / g);
+  }
 }
 
 __device__ __forceinline__ Pass make_pass(const FusedArgs& a, const Ctrl& cb, const int* table, int pass) {
   Pass P;
-  const int S = cb.S;
   P.per = units_per_segment(a, pass);
-  unit_range(S * P.per, P.ub, P.ue);
+  P.ub = cb.ub[pass];  // set by build_table
+  P.ue = cb.ue[pass];
   P.seg_first = cb.seg_first[pass];
   P.table = cb.cached[pass] ? table + pass * kWsCache * kWsInts : a.wseg + static_cast<size_t>(P.seg_first) * kWsInts;
   return P;
@@ -691,6 +697,8 @@ __device__ void build_table(const FusedArgs& a, Ctrl& cb, int* table, int* scrat
     if (tid == 0) {
       cb.seg_first[pass] = first[pass];
       cb.cached[pass] = cached[pass];
+      cb.ub[pass] = ub;
+      cb.ue[pass] = ue;
     }
   }
   for (int i = tid; i < n[0] + n[1]; i += nt) {
