@@ -1394,9 +1394,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(FusedArgs a) {
   }
   const int quads = a.H / 4;
   const int64_t total = static_cast<int64_t>(a.M) * quads;
-  const int64_t b = total * blockIdx.x / gridDim.x, e = total * (blockIdx.x + 1) / gridDim.x;
+  int64_t b, e;  // this CTA's slice; 32-bit arithmetic unless the output is huge
+  if (total <= 0x7fffffff) {
+    int b32, e32;
+    unit_range(static_cast<int>(total), b32, e32);
+    b = b32;
+    e = e32;
+  } else {
+    b = total * blockIdx.x / gridDim.x;
+    e = total * (blockIdx.x + 1) / gridDim.x;
+  }
   // (token, quad) of element i carried along, one division per thread
-  int ctok = static_cast<int>((b + threadIdx.x) / quads), cq = static_cast<int>((b + threadIdx.x) % quads);
+  const int64_t i0 = b + threadIdx.x;
+  int ctok, cq;
+  if (i0 <= 0x7fffffff) {
+    ctok = static_cast<int>(i0) / quads;
+    cq = static_cast<int>(i0) % quads;
+  } else {
+    ctok = static_cast<int>(i0 / quads);
+    cq = static_cast<int>(i0 % quads);
+  }
   const int dtok = kThreads / quads, dq = kThreads % quads;
   for (int64_t i = b + threadIdx.x; i < e; i += kThreads, ctok += dtok, cq += dq, ctok += cq >= quads, cq -= cq >= quads ? quads : 0) {
     const int tok = ctok;
