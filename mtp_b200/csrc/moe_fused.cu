@@ -1,5 +1,5 @@
 // The W4A16 MoE layer forward on sm_100a as one persistent kernel (one CTA
-// per SM, 15 warps). It runs in three phases separated by grid-wide barriers:
+// per SM, 16 warps). It runs in three phases separated by grid-wide barriers:
 //
 //   routing  CTA c routes tokens c, c + G, ... (G = CTAs): router softmax /
 //            top-k / renormalise (warps 0-6, one token each) and the shared
