@@ -110,3 +110,23 @@ def test_python_api_rejects_cpu_tensors(built_lib):
         mtp_b200.topk_softmax(torch.zeros(2, 8), 2)
     with pytest.raises(ValueError):
         mtp_b200.moe_align_block_size(torch.zeros(2, 2, dtype=torch.int32), 8, 8)
+    # the product entry points have no CPU path: host tensors are refused
+    # before anything runs
+    from mtp_b200.ops import MtpPredictor, W4A16Experts, dequantize_gptq_projection, moe_layer_w4a16
+    i32 = dict(dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        dequantize_gptq_projection(torch.zeros(16, 8, **i32), torch.zeros(1, 1, **i32),
+                                   torch.zeros(1, 8, dtype=torch.float16))
+    with pytest.raises(ValueError, match="CUDA"):
+        W4A16Experts.from_gptq(torch.zeros(2, 32, 256, **i32), torch.zeros(2, 2, 32, **i32),
+                               torch.zeros(2, 2, 256, dtype=torch.float16), torch.zeros(2, 16, 256, **i32),
+                               torch.zeros(2, 1, 32, **i32), torch.zeros(2, 1, 256, dtype=torch.float16))
+    experts = W4A16Experts(None, 2, 256, 128, 128, None)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe_layer_w4a16(torch.zeros(4, 256, dtype=torch.bfloat16), torch.zeros(4, 2), experts, 1)
+    with pytest.raises(ValueError, match="CUDA"):
+        mtp_b200.fused_experts(torch.zeros(4, 256, dtype=torch.bfloat16), experts,
+                               topk_weights=torch.ones(4, 1), topk_ids=torch.zeros(4, 1, **i32))
+    with pytest.raises(ValueError, match="CUDA"):
+        MtpPredictor(torch.zeros(64, 256, dtype=torch.bfloat16), None, torch.zeros(8, 64, dtype=torch.bfloat16),
+                     None, future=1, experts=8)
